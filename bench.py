@@ -1,0 +1,461 @@
+"""Benchmark of the nerf_b200 training hot path (train samples/s) on 1..8 B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (bounded training): a seeded procedural scene of 12
+spheres/boxes with value-noise albedo in [-1.5,1.5]^3, 100 training views at
+800x800 rendered exactly on the host (stands in for the Blender dataset);
+hash grid L16 F2 T=2^19 N_max=2048; <= 1024 steps per ray; 2^18 target
+compacted samples per step per GPU; 128^3 occupancy refreshed every 16 steps;
+random background; Adam lr 1e-2, betas 0.9/0.99, eps 1e-15.  One "step" is
+one nerf_train_step.  The timed steps run after an untimed pretrain past the
+occupancy warm-up, so they measure steady-state training.
+
+value: compacted samples trained per second over all ranks (device time, CUDA
+events on each context's stream, max over ranks).  e2e: the same metric for
+a whole job through the C ABI from pinned host memory: create (uploads the
+images), configure, then every step nerf_train_step + nerf_read_train_stats
+(20-byte device-to-host read).  Extra keys: roofline of the dominant kernel
+from event-timed kernel-by-kernel steps, per-kernel times, render MRays/s
+(config 3), cpu_baseline (the CPU oracle on a bounded sample).
+
+--impl reference times the reference algorithm's CPU implementation (the
+oracle port; the reference backend has no CPU path) on the host cores, rank 0
+only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+# ---------------------------------------------------------------- workload
+CFG2 = dict(kind=1, seed=2, n_primitives=12, density=100.0, extent=1.0, size_min=0.1, size_max=0.6, n_views=100,
+            width=800, height=800, fov=0.69, radius=4.0, camera_mode=1)
+AABB2 = ((-1.5, -1.5, -1.5), (1.5, 1.5, 1.5))
+TARGET_SAMPLES = 1 << 18
+MAX_STEPS_PER_RAY = 1024
+GRID_RES = 128
+WORKLOAD = ("config2 bounded training: 12 spheres/boxes, 100 views 800x800, hash L16 F2 T2^19 Nmax2048, "
+            "2^18 target samples/step/GPU, <=1024 steps/ray, 128^3 occupancy every 16 steps, random bg")
+
+
+def options(nb, **kw):
+    return nb.default_options(log2_hashmap_size=19, max_resolution=2048, background=1, stop_transmittance=1e-4,
+                              target_samples_per_step=TARGET_SAMPLES, max_samples_per_step=2 * TARGET_SAMPLES, **kw)
+
+
+def train_config(nb):
+    return nb.training_config(aabb=AABB2, rays=4096, steps=MAX_STEPS_PER_RAY, lr=1e-2, beta1=0.9, beta2=0.99,
+                              eps=1e-15, clip=1e9, guard=1e12, loss_scale=128.0, lr_decay_ksteps=0, decay=0.95,
+                              threshold=0.01, cells_per_update=GRID_RES ** 3, update_interval=16, warmup=256)
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in self.lines:
+            parts = [x.strip() for x in l.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_dataset(nb, views=None):
+    cfg = dict(CFG2)
+    if views is not None:
+        cfg["n_views"] = views
+    t0 = time.time()
+    ds = nb.make_scene(**cfg)
+    return ds, time.time() - t0
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import ctypes as C
+
+    import torch
+    import torch.distributed as dist
+
+    import nerf_b200 as nb
+    from nerf_b200 import abi
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=__import__("datetime").timedelta(seconds=300))
+
+    lib = abi.load()
+    ds, gen_s = make_dataset(nb, args.views)
+    pinned_imgs = torch.from_numpy(ds.images).pin_memory()  # host buffer of the e2e job
+    ds_pinned = nb.Dataset(pinned_imgs.numpy(), ds.cameras, ds.intrinsics)
+
+    ctx = nb.Context(ds, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
+                     options=options(nb))
+    uid = None
+    if world > 1:
+        obj = [nb.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+        ctx.dp_init(rank, world, uid)
+    ctx.configure(train_config(nb))
+    sp = C.c_void_p()
+    abi.check("stream", lib.nerf_b200_context_stream(ctx.handle, C.byref(sp)))
+    stream = torch.cuda.ExternalStream(sp.value)
+
+    for _ in range(args.pretrain):
+        ctx.train_step()
+    for _ in range(args.warmup):
+        ctx.train_step()
+    c0 = ctx.counters()
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        ctx.train_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    if world > 1:
+        dist.barrier()
+    c1 = ctx.counters()
+    samples = c1.total_samples - c0.total_samples
+    rays = c1.total_rays - c0.total_rays
+    t = torch.tensor([ms, float(samples), float(rays)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        tsum = t.clone()
+        dist.all_reduce(tsum, op=dist.ReduceOp.SUM)
+        ms_max, samples_all, rays_all = float(tmax[0]), float(tsum[1]), float(tsum[2])
+    else:
+        ms_max, samples_all, rays_all = ms, float(samples), float(rays)
+    value = samples_all / (ms_max / 1e3)
+    stats = ctx.stats()
+
+    # Kernel-by-kernel timing of the same step (events between launches).
+    prof = np.zeros(10)
+    n_prof = args.profile_steps
+    prof_samples = 0
+    for _ in range(n_prof):
+        cb = ctx.counters()
+        p = abi.NerfB200StepProfile()
+        abi.check("profiled step", lib.nerf_b200_train_step_profiled(ctx.handle, C.byref(p)))
+        prof += np.array(p.milliseconds[:])
+        prof_samples += ctx.counters().total_samples - cb.total_samples
+    prof /= max(1, n_prof)
+    mean_samples = prof_samples / max(1, n_prof)
+    kernels = kernel_table(ctx, prof, mean_samples)
+
+    render = None
+    if not args.skip_render:
+        render = run_render(nb, ctx, rank, world, args)
+
+    e2e = None
+    if not args.skip_e2e:
+        ctx.close()
+        torch.cuda.synchronize()
+        e2e = run_e2e(nb, lib, ds_pinned, rank, world, uid, args)
+
+    cpu = None
+    if rank == 0 and not args.skip_cpu:
+        cpu = cpu_baseline(nb, ds, args)
+
+    if rank == 0:
+        hbm, src = peaks()
+        dom = max(kernels, key=lambda k: k["ms"])
+        line = {
+            "metric": "train samples/s (config 2, steady state)",
+            "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f16 (fp32 accumulate, fp32 Adam masters)", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "parallelism": f"dp{world}", "pretrain_steps": args.pretrain,
+                       "samples_per_step": samples_all / args.steps, "rays_per_step": rays_all / args.steps,
+                       "l2": "inputs larger than L2: each step streams the 171 MB fp32 master/m/v through Adam and "
+                             "reads a 256 MB image set; the 24 MB hash table is meant to stay L2-resident",
+                       "final_loss": stats.loss, "dataset_gen_s": gen_s},
+            "e2e": e2e,
+            "gpu_launches": 11 * args.steps,
+            "roofline": roofline(dom, hbm, src),
+            "kernels": kernels,
+            "render": render,
+            "cpu_baseline": cpu,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def kernel_table(ctx, prof_ms, samples):
+    """Algorithmic bytes per launch for each step kernel (DESIGN.md lists the per-unit figures)."""
+    from nerf_b200 import abi
+    n_params = ctx.n_params
+    n_grid = ctx.n_grid
+    cells = GRID_RES ** 3
+    per = {
+        # stored features 64 + dout 16 + pos/dt 16 + ray id 4, and 128 f16x2 read-modify-writes of 4+4 bytes
+        "field_backward": samples * (64 + 16 + 16 + 4 + 128 * 8),
+        # pos/dt 16 + ray id 4 + 128 gathers of 4 bytes + features 64 + raw outputs 16
+        "field_forward": samples * (16 + 4 + 128 * 4 + 64 + 16),
+        # raw 16 + pos/dt 16 read twice, dout 16 written (T parked in dout.x: +4+4)
+        "composite": samples * (2 * 32 + 16 + 8),
+        # fp32 master, m, v read+write (24), fp16 grad read + cleared (4 grid) , fp16 param write (2)
+        "adam": n_grid * 30 + (n_params - n_grid) * 30,
+        "grad_stats": n_grid * 2 + (n_params - n_grid) * 4,
+        "wgrad_reduce": (ctx_partials(ctx) + 1) * 10240 * 4,
+        "occupancy_update": cells * 8 + cells // 8,
+        "sampler": samples * (16 + 4) * 1,
+        "occupancy_query": 0,
+        "allreduce": n_grid * 2 + 10248 * 4,
+    }
+    out = []
+    for name, ms in zip(abi.STEP_KERNELS, prof_ms):
+        b = per.get(name, 0)
+        out.append({"kernel": name, "ms": float(ms), "bytes": int(b), "gbs": (b / (ms / 1e3) / 1e9) if ms > 0 else 0.0})
+    return out
+
+
+def ctx_partials(ctx):
+    from nerf_b200 import abi
+    return int(abi.load().nerf_b200_field_backward_partial_floats()) // 10240
+
+
+def roofline(dom, hbm, src):
+    achieved = dom["gbs"]
+    return {"kernel": dom["kernel"], "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+            "frac": achieved / hbm, "peak_source": src,
+            "traffic": None, "note": "achieved = algorithmic bytes per launch / mean CUDA-event launch time "
+                                     "(kernel-by-kernel step, same kernels as the graph); traffic from ncu in profiles/"}
+
+
+def run_render(nb, ctx, rank, world, args):
+    """Config 3: config-2 architecture, seeded random-init weights, fixed 30% Bernoulli(seed 1) occupancy,
+    orbit views at radius 4 (800x800), T < 1e-4 termination, 64x64 tiles round-robin over the ranks."""
+    import torch
+    import torch.distributed as dist
+    ds = ctx.ds
+    views = nb.make_scene(**{**CFG2, "n_views": args.render_views, "camera_mode": 2, "orbit_elevation": 0.35,
+                             "orbit_views": 200, "view_offset": 0}, with_images=False)
+    rctx = nb.Context(nb.Dataset(ds.images[:1], ds.cameras[:1], ds.intrinsics), grid_res=GRID_RES,
+                      max_sample_steps=1 << 16, max_batch_rays=4096, options=options(nb))
+    rctx.configure(train_config(nb))
+    rng = np.random.default_rng(1)
+    bits = np.packbits(rng.random(GRID_RES ** 3) < 0.3, bitorder="little").view(np.uint32)
+    rctx.set_occupancy(bitfield=bits)
+    W, H = 800, 800
+    for v in range(min(2, args.render_views)):  # warm-up
+        rctx.render(views.cameras[v], W, H, views.intrinsics, max_steps=MAX_STEPS_PER_RAY, stop=1e-4, tile=64, rank=rank,
+                    world=world)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    ms = 0.0
+    rays = samples = 0
+    for v in range(args.render_views):
+        info = rctx.render(views.cameras[v], W, H, views.intrinsics, max_steps=MAX_STEPS_PER_RAY, stop=1e-4, tile=64,
+                           rank=rank, world=world)
+        ms += info.milliseconds
+        rays += info.rays
+        samples += info.samples
+    wall = time.time() - t0
+    t = torch.tensor([ms, float(rays), float(samples)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        tm = t.clone()
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ts = t.clone()
+        dist.all_reduce(ts, op=dist.ReduceOp.SUM)
+        ms, rays, samples = float(tm[0]), float(ts[1]), float(ts[2])
+    rctx.close()
+    return {"metric": "render MRays/s (config 3)", "value": rays / (ms / 1e3) / 1e6, "unit": "MRays/s",
+            "views": args.render_views, "resolution": "800x800", "samples_per_ray": samples / max(rays, 1),
+            "device_ms": ms, "wall_s": wall, "tiles": "64x64 round-robin over ranks"}
+
+
+def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
+    """Whole job through the C ABI with host buffers: create (uploads the pinned images), configure, and each step
+    nerf_train_step + nerf_read_train_stats.  Samples come from the additive counters export."""
+    import torch
+    import torch.distributed as dist
+    steps = args.e2e_steps
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    ctx = nb.Context(ds_pinned, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
+                     options=options(nb))
+    if world > 1:
+        ctx.dp_init(rank, world, uid if rank == 0 else uid)
+    ctx.configure(train_config(nb))
+    for _ in range(steps):
+        ctx.train_step()
+        ctx.stats()
+    t1 = time.perf_counter()
+    c = ctx.counters()
+    ctx.close()
+    t = torch.tensor([t1 - t0, float(c.total_samples)], dtype=torch.float64, device="cuda")
+    if world > 1:
+        tm = t.clone()
+        dist.all_reduce(tm, op=dist.ReduceOp.MAX)
+        ts = t.clone()
+        dist.all_reduce(ts, op=dist.ReduceOp.SUM)
+        secs, samples = float(tm[0]), float(ts[1])
+    else:
+        secs, samples = float(t[0]), float(t[1])
+    h2d = ds_pinned.images.nbytes + ds_pinned.cameras.nbytes
+    return {"value": samples / secs, "unit": "samples/s", "steps": steps, "seconds": secs,
+            "h2d_bytes_per_step": h2d / steps, "d2h_bytes_per_step": 20,
+            "note": "create+upload, configure and every step train_step + read_train_stats, wall clock, max over ranks; "
+                    "includes the occupancy warm-up phase of a fresh job"}
+
+
+def cpu_baseline(nb, ds, args, steps=None, threads=None, seconds=20.0):
+    """The CPU oracle (restatement of the same algorithm) on a bounded sample of the config-2 workload."""
+    from oracle import oracle
+    threads = threads or os.cpu_count() or 1
+    opts = options(nb)
+    desc = nb.Context.__new__(nb.Context)
+    images = np.ascontiguousarray(ds.images)
+    cams = np.ascontiguousarray(ds.cameras)
+    fx, fy, cx, cy = ds.intrinsics
+    from nerf_b200.abi import NerfCreateDesc
+    d = NerfCreateDesc(GRID_RES, 2 * TARGET_SAMPLES, 1 << 16, 256, images.ctypes.data, images.nbytes, cams.ctypes.data,
+                       cams.nbytes, ds.n, ds.width, ds.height, fx, fy, cx, cy)
+    # bounded sample: 1/64 of the per-step sample target, same rays-per-step rule
+    small = TARGET_SAMPLES // 64
+    oc = oracle.Context(d, oracle.options(log2_hashmap_size=19, max_resolution=2048, background=1,
+                                          stop_transmittance=1e-4, target_samples_per_step=small,
+                                          max_samples_per_step=2 * small, n_threads=threads), images, cams)
+    cfg = train_config(nb)
+    cfg.rays_per_batch = 64
+    oc.configure(cfg)
+    t0 = time.perf_counter()
+    samples = 0
+    n = 0
+    while True:
+        oc.step()
+        samples += oc.info().samples
+        n += 1
+        if (steps and n >= steps) or (not steps and time.perf_counter() - t0 > seconds):
+            break
+    dt = time.perf_counter() - t0
+    oc.close()
+    return {"value": samples / dt, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{n} oracle training steps of config 2 at {small} target samples/step ({samples} samples, "
+                      f"{dt:.1f} s, warm-up phase of a fresh job)"}
+
+
+# ------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import nerf_b200 as nb
+    ds, _ = make_dataset(nb, args.views)
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        pass
+    res = cpu_baseline(nb, ds, args, steps=max(1, args.steps), threads=threads)
+    line = {"metric": "train samples/s (config 2, steady state)", "value": res["value"], "unit": "samples/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 (fp16-rounded operands)", "data": "synthetic", "impl": "reference",
+            "config": {"workload": WORKLOAD, "parallelism": "cpu"},
+            "cpu_baseline": res,
+            "e2e": {"value": res["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--pretrain", type=int, default=400)
+    ap.add_argument("--profile-steps", type=int, default=20)
+    ap.add_argument("--render-views", type=int, default=20)
+    ap.add_argument("--e2e-steps", type=int, default=1000)
+    ap.add_argument("--views", type=int, default=None)
+    ap.add_argument("--skip-render", action="store_true")
+    ap.add_argument("--skip-e2e", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,110 @@
+// grid.cuh -- multiresolution hash-grid corner math, gather and scatter.
+//
+// Level l has scale s_l, R_l vertices per axis, and a dense or hashed table
+// starting at entry offset_l (see grid_layout() in context.cu).  A unit-cube
+// point p maps to u = fma(clamp01(p), s_l, 0.5) per axis, the cell corner
+// i = clamp(floor(u), 0, R_l - 2) and the fraction f = u - floor(u).  Corner c
+// (bit 0 = x, bit 1 = y, bit 2 = z) has weight ((wx*wy)*wz), w = f or 1-f,
+// and entry x + R(y + Rz) on dense levels or
+// (x ^ y*2654435761 ^ z*805459861) & (T-1) on hashed levels.  Each entry holds
+// two fp16 features; the forward value is fma-accumulated over c = 0..7 from
+// zero and rounded once to fp16.  Every operation is written with an explicit
+// rounding intrinsic so that the CPU oracle reproduces indices, weights and
+// forward features bit for bit.
+#pragma once
+#include "common.cuh"
+
+namespace nb {
+
+struct alignas(16) LevelParams {
+    float scale;
+    uint32_t res;
+    uint32_t dense;
+    uint32_t offset;
+};
+
+NB_DEV float clamp01(float x) { return fminf(1.0f, fmaxf(0.0f, x)); }
+
+NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_mask, uint32_t idx[8], float w[8]) {
+    uint32_t i[3];
+    float f[3];
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        const float u = __fmaf_rn(clamp01(p[d]), lp.scale, 0.5f);
+        const float fl = floorf(u);
+        f[d] = __fsub_rn(u, fl);
+        int ii = static_cast<int>(fl);
+        ii = max(0, min(static_cast<int>(lp.res) - 2, ii));
+        i[d] = static_cast<uint32_t>(ii);
+    }
+    const float g0[3] = {__fsub_rn(1.0f, f[0]), __fsub_rn(1.0f, f[1]), __fsub_rn(1.0f, f[2])};
+#pragma unroll
+    for (uint32_t c = 0; c < 8u; ++c) {
+        const uint32_t cx = i[0] + (c & 1u), cy = i[1] + ((c >> 1) & 1u), cz = i[2] + ((c >> 2) & 1u);
+        const uint32_t e = lp.dense ? cx + lp.res * (cy + lp.res * cz)
+                                    : ((cx ^ (cy * 2654435761u) ^ (cz * 805459861u)) & hash_mask);
+        idx[c] = lp.offset + e;
+        const float wx = (c & 1u) ? f[0] : g0[0];
+        const float wy = (c & 2u) ? f[1] : g0[1];
+        const float wz = (c & 4u) ? f[2] : g0[2];
+        w[c] = __fmul_rn(__fmul_rn(wx, wy), wz);
+    }
+}
+
+// Interpolated feature pair of one level (packed f16x2).  params: one
+// uint32 (two fp16 features) per entry.
+NB_DEV uint32_t level_forward(const uint32_t* __restrict__ params, const float p[3], const LevelParams lp, uint32_t hash_mask) {
+    uint32_t idx[8];
+    float w[8];
+    level_corners(p, lp, hash_mask, idx, w);
+    uint32_t v[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) v[c] = __ldg(params + idx[c]);
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float2 f = unpack_h2(v[c]);
+        a0 = __fmaf_rn(w[c], f.x, a0);
+        a1 = __fmaf_rn(w[c], f.y, a1);
+    }
+    return pack_h2(a0, a1);
+}
+
+// Two (point, level) tasks with all 16 gathers issued before any is used.
+NB_DEV void level_forward2(const uint32_t* __restrict__ params, const float pa[3], const LevelParams la, const float pb[3],
+                           const LevelParams lb, uint32_t hash_mask, uint32_t& ra, uint32_t& rb) {
+    uint32_t ia[8], ib[8];
+    float wa[8], wb[8];
+    level_corners(pa, la, hash_mask, ia, wa);
+    level_corners(pb, lb, hash_mask, ib, wb);
+    uint32_t va[8], vb[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        va[c] = __ldg(params + ia[c]);
+        vb[c] = __ldg(params + ib[c]);
+    }
+    float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        const float2 fa = unpack_h2(va[c]);
+        const float2 fb = unpack_h2(vb[c]);
+        a0 = __fmaf_rn(wa[c], fa.x, a0);
+        a1 = __fmaf_rn(wa[c], fa.y, a1);
+        b0 = __fmaf_rn(wb[c], fb.x, b0);
+        b1 = __fmaf_rn(wb[c], fb.y, b1);
+    }
+    ra = pack_h2(a0, a1);
+    rb = pack_h2(b0, b1);
+}
+
+// Scatter of one level's feature gradient (d0, d1) to the eight corner
+// entries with fp16x2 reductions performed at L2.
+NB_DEV void level_backward(uint32_t* grad, const float p[3], const LevelParams lp, uint32_t hash_mask, float d0, float d1) {
+    uint32_t idx[8];
+    float w[8];
+    level_corners(p, lp, hash_mask, idx, w);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) red_add_f16x2(grad + idx[c], pack_h2(w[c] * d0, w[c] * d1));
+}
+
+}  // namespace nb

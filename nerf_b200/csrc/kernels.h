@@ -1,0 +1,158 @@
+// kernels.h -- launch interface of the sm_100a kernels (internal to libnerf_b200).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "types.h"
+
+namespace nb {
+
+struct alignas(16) LevelTable {
+    // scale, res, dense, offset per level (LevelParams layout)
+    float scale[kMaxLevels];
+    uint32_t res[kMaxLevels];
+    uint32_t dense[kMaxLevels];
+    uint32_t offset[kMaxLevels];
+    uint32_t n_levels;
+    uint32_t hash_mask;
+};
+LevelTable make_level_table(const GridLayout& g);
+
+// ---- standalone hash-grid encoder (unit-cube points, any level count) ----
+cudaError_t launch_grid_forward(const LevelTable& lt, const float* pos_unit, uint32_t n, const void* params,
+                                void* feat, cudaStream_t s);
+cudaError_t launch_grid_backward(const LevelTable& lt, const float* pos_unit, uint32_t n, const void* dfeat_f16,
+                                 void* grad_f16, cudaStream_t s);
+
+// ---- fused field (hash grid L=16 + density/colour MLPs) ----
+enum FieldMode : int { kFieldTrain = 0, kFieldOccupancy = 1, kFieldDirect = 2 };
+struct FieldArgs {
+    LevelTable lt;
+    const void* params16;   // flat fp16 parameters (grid entries, then MLP)
+    uint32_t mlp_offset;    // index of the first MLP parameter
+    uint32_t n_direct;      // rows for kFieldDirect
+    DeviceState* state;
+    // training rows
+    const float4* pos_dt;
+    const uint32_t* sample_ray;
+    const RayRecord* rays;
+    float aabb_min[3], aabb_max[3], aabb_size[3];
+    // occupancy rows
+    uint32_t grid_res, cell_count, update_count, warmup_steps, update_interval;
+    float* occ_sigma;
+    // direct rows
+    const float* pos_unit;
+    const float* dirs;
+    // outputs / inputs
+    void* feat;            // fp16 n x 32 (forward writes, backward reads)
+    float4* raw;           // forward: raw sigma, raw rgb
+    const float4* dout;    // backward: loss-scaled d raw
+    void* grid_grad;       // backward: fp16 entries x 2 (reduction target)
+    float* partials;       // backward: [grid][kMlpParams] per-CTA weight gradients
+};
+cudaError_t launch_field_forward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
+cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
+uint32_t field_forward_blocks();
+uint32_t field_backward_blocks();
+cudaError_t field_init_attributes();
+
+// ---- sampler ----
+struct SamplerArgs {
+    TrainConsts tc;
+    DeviceState* state;
+    const float* cams;
+    const uint8_t* images;
+    const uint32_t* bitfield;
+    uint32_t* ray_counts;     // [max_rays]
+    uint32_t* masks;          // [mask_words][max_rays]
+    uint32_t* block_samples;  // [blocks]
+    uint32_t* block_active;   // [blocks]
+    RayRecord* rays;          // [max_rays] compacted
+    float4* pos_dt;           // [sample_cap]
+    uint32_t* sample_ray;     // [sample_cap]
+    uint32_t* ray_index;      // [max_rays] compacted -> marched ray index
+};
+constexpr uint32_t kSamplerBlock = 128;
+cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s);
+
+// ---- compositing + loss ----
+struct CompositeArgs {
+    const RayRecord* rays;
+    const float4* raw;
+    const float4* pos_dt;
+    float4* dout;
+    DeviceState* state;
+    float* loss_slot;     // MLP-gradient buffer slot of the loss sum
+    uint32_t max_rays;
+    uint32_t dp_world;
+    float loss_scale;
+    float stop_transmittance;
+    // direct mode (tests): explicit ray count and normaliser
+    int direct;
+    uint32_t n_rays;
+    float inv_norm;
+    float* ray_loss;      // optional per-ray loss
+    uint32_t* ray_used;   // optional per-ray samples used
+};
+cudaError_t launch_composite(const CompositeArgs& a, cudaStream_t s);
+
+// ---- occupancy ----
+struct OccupancyArgs {
+    DeviceState* state;
+    float* density;
+    uint32_t* bitfield;
+    const float* occ_sigma;
+    uint32_t cell_count, update_count, warmup_steps, update_interval;
+    float decay, threshold;
+    int direct;             // 1: use `mode` and `frame` below instead of the device state
+    uint32_t mode, frame;
+};
+cudaError_t launch_occupancy_update(const OccupancyArgs& a, cudaStream_t s);
+
+// ---- optimiser ----
+struct OptimArgs {
+    TrainConsts tc;
+    DeviceState* state;
+    float* master;
+    void* params16;
+    void* grid_grad;         // fp16 [n_grid]
+    float* mlp_grad;         // fp32 [kMlpGradSlots]
+    float* m;
+    float* v;
+    const float* partials;
+    uint32_t n_partials;
+    uint64_t n_grid;         // grid parameters (multiple of 16)
+    uint64_t n_params;       // grid + MLP
+    uint32_t stats_blocks;
+    AdamScalars direct_scalars;  // used when state is null (kernel-level entry point)
+};
+cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s);
+cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);
+cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s);
+uint32_t grad_stats_blocks(uint64_t n_params);
+cudaError_t launch_f32_to_f16(const float* src, void* dst, uint64_t n, cudaStream_t s);
+
+// ---- render ----
+struct RenderArgs {
+    LevelTable lt;
+    const void* params16;
+    uint32_t mlp_offset;
+    const uint32_t* bitfield;
+    uint32_t grid_res;
+    float aabb_min[3], aabb_max[3], aabb_size[3];
+    float c2w[12];
+    uint32_t width, height;
+    float fx, fy, cx, cy;
+    uint32_t max_steps;
+    float stop_transmittance;
+    uint32_t tile, tile_rank, tile_world;  // 0 tile: whole image on this rank
+    uint32_t* rgba;             // width*height packed RGBA8
+    uint32_t* spp;              // optional samples per pixel
+    uint32_t* work_counter;     // device counter for dynamic pixel scheduling
+    unsigned long long* total_samples;  // optional
+};
+cudaError_t launch_render(const RenderArgs& a, cudaStream_t s);
+cudaError_t render_init_attributes();
+
+}  // namespace nb

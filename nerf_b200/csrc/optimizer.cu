@@ -1,0 +1,258 @@
+// optimizer.cu -- end of a training step.
+//
+//   k_wgrad_reduce  sums the per-CTA MLP weight-gradient partials of the
+//                   backward kernel (deterministic order).
+//   k_grad_stats    sum of squares and non-finite flag over all gradients
+//                   (fp16 hash-table part, fp32 MLP part); the last block to
+//                   finish derives the step statistics, the update guard,
+//                   the clip scale, the learning-rate decay and the bias
+//                   corrections, and commits the step (reference
+//                   backend-cuda.cu:1451-1536: grad stats, finalize, Adam
+//                   scalars and commit, folded into one launch).
+//   k_adam          Adam on fp32 masters with the fp16 mirror, one pass over
+//                   the flat parameter vector, 8 parameters per thread; the
+//                   hash-table gradients are cleared behind it for the next
+//                   step (reference backend-cuda.cu:1537-1554).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace nb {
+namespace {
+
+__global__ void __launch_bounds__(256) k_wgrad_reduce(const float* __restrict__ partials, uint32_t n_partials, float* mlp_grad) {
+    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= kMlpParams) return;
+    float s = 0.0f;
+    for (uint32_t c = 0; c < n_partials; ++c) s += partials[static_cast<unsigned long long>(c) * kMlpParams + i];
+    mlp_grad[i] = s;
+}
+
+__device__ __forceinline__ void adam_scalars(const TrainConsts& tc, float grad_norm, uint32_t nonfinite, uint32_t step,
+                                             AdamScalars& o) {
+    const bool skip = nonfinite != 0u || !isfinite(grad_norm) || grad_norm > tc.guard;
+    o.learning_rate = 0.0f;
+    o.grad_scale = 1.0f;
+    o.inv_bias_correction1 = 1.0f;
+    o.inv_bias_correction2 = 1.0f;
+    if (!skip) {
+        const float decay = static_cast<float>(tc.lr_decay_ksteps) * 1000.0f;
+        o.learning_rate = decay > 0.0f ? tc.lr * powf(0.1f, static_cast<float>(step) / decay) : tc.lr;
+        o.grad_scale = grad_norm > tc.clip && grad_norm > 0.0f ? tc.clip / grad_norm : 1.0f;
+        o.inv_bias_correction1 = 1.0f / (1.0f - powf(tc.beta1, static_cast<float>(step)));
+        o.inv_bias_correction2 = 1.0f / (1.0f - powf(tc.beta2, static_cast<float>(step)));
+    }
+    o.inv_loss_scale = 1.0f / tc.loss_scale;
+    o.skip_update = skip ? 1u : 0u;
+}
+
+__global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
+    const uint64_t n_chunks = a.n_params / 8u;
+    const uint64_t grid_chunks = a.n_grid / 8u;
+    const uint4* gg = static_cast<const uint4*>(a.grid_grad);
+    float sum = 0.0f;
+    uint32_t bad = 0u;
+    for (uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n_chunks;
+         q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        float v[8];
+        if (q < grid_chunks) {
+            const uint4 u = gg[q];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = unpack_h2(w[k]);
+                v[2 * k] = f.x;
+                v[2 * k + 1] = f.y;
+            }
+        } else {
+            const float4* mg = reinterpret_cast<const float4*>(a.mlp_grad + 8u * (q - grid_chunks));
+            const float4 x = mg[0], y = mg[1];
+            v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
+            v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (!isfinite(v[k])) bad = 1u;
+            else sum = fmaf(v[k], v[k], sum);
+        }
+    }
+    __shared__ float ps[8];
+    __shared__ uint32_t pb[8];
+    __shared__ bool last;
+    const float ws = warp_sum(sum);
+    const uint32_t wb = __any_sync(0xffffffffu, bad != 0u) ? 1u : 0u;
+    if ((threadIdx.x & 31u) == 0u) {
+        ps[threadIdx.x >> 5] = ws;
+        pb[threadIdx.x >> 5] = wb;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0u) {
+        float bs = 0.0f;
+        uint32_t bb = 0u;
+        for (uint32_t w = 0; w < blockDim.x / 32u; ++w) {
+            bs += ps[w];
+            bb |= pb[w];
+        }
+        if (bs != 0.0f) atomicAdd(&a.state->grad_sumsq, bs);
+        if (bb) atomicOr(&a.state->nonfinite, 1u);
+        __threadfence();
+        last = atomicAdd(&a.state->done_blocks, 1u) == gridDim.x - 1u;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0u) return;
+    __threadfence();
+    DeviceState* st = a.state;
+    const TrainConsts& tc = a.tc;
+    const float sumsq = atomicAdd(&st->grad_sumsq, 0.0f);
+    const uint32_t nonfinite = atomicOr(&st->nonfinite, 0u);
+    const float loss = *reinterpret_cast<volatile float*>(a.mlp_grad + kMlpGradLoss);
+    const float grad_norm = sqrtf(fmaxf(0.0f, sumsq)) / tc.loss_scale;
+    const uint32_t has_nonfinite = (nonfinite != 0u || !isfinite(loss) || !isfinite(grad_norm)) ? 1u : 0u;
+    const uint32_t frame = st->frame_index;
+    const uint32_t step = frame + 1u;
+    st->stats.loss = loss;
+    st->stats.grad_norm = grad_norm;
+    st->stats.has_nonfinite = has_nonfinite;
+    st->stats.completed_steps = step;
+    st->stats.last_train_camera = train_camera(frame, tc.n_images);
+    AdamScalars sc;
+    adam_scalars(tc, grad_norm, has_nonfinite, step, sc);
+    st->adam = sc;
+    const uint32_t samples = st->n_samples, rays = st->n_rays;
+    st->last_samples = samples;
+    st->last_active = st->n_active;
+    st->last_rays = rays;
+    st->total_samples += samples;
+    st->total_rays += rays;
+    if (tc.target_samples != 0u) {
+        unsigned long long next = samples == 0u ? 2ull * rays
+                                                : static_cast<unsigned long long>(rays) * tc.target_samples / samples;
+        next = next < 128ull ? 128ull : next;
+        next = next > tc.max_rays ? tc.max_rays : next;
+        st->n_rays = static_cast<uint32_t>(next);
+    }
+    st->frame_index = step;
+    st->grad_sumsq = 0.0f;
+    st->nonfinite = 0u;
+    st->done_blocks = 0u;
+    a.mlp_grad[kMlpGradLoss] = 0.0f;
+}
+
+// Adam for 8 consecutive parameters; g holds the loss-scaled gradients.
+__device__ __forceinline__ void adam8(float* master, __half* p16, float* m, float* v, const float g[8], const AdamScalars& s,
+                                      float b1, float b2, float eps) {
+    float4* M4 = reinterpret_cast<float4*>(master);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    float W[8], Mm[8], Vv[8];
+    *reinterpret_cast<float4*>(W) = M4[0];
+    *reinterpret_cast<float4*>(W + 4) = M4[1];
+    *reinterpret_cast<float4*>(Mm) = m4[0];
+    *reinterpret_cast<float4*>(Mm + 4) = m4[1];
+    *reinterpret_cast<float4*>(Vv) = v4[0];
+    *reinterpret_cast<float4*>(Vv + 4) = v4[1];
+    const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
+    uint32_t h[4];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        const float gk = __fmul_rn(__fmul_rn(g[k], s.inv_loss_scale), s.grad_scale);
+        const float mi = __fadd_rn(__fmul_rn(b1, Mm[k]), __fmul_rn(omb1, gk));
+        const float vi = __fadd_rn(__fmul_rn(b2, Vv[k]), __fmul_rn(__fmul_rn(omb2, gk), gk));
+        const float num = __fmul_rn(s.learning_rate, __fmul_rn(mi, s.inv_bias_correction1));
+        const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vi, s.inv_bias_correction2)), eps);
+        const float w = __fsub_rn(W[k], __fdiv_rn(num, den));
+        W[k] = w;
+        Mm[k] = mi;
+        Vv[k] = vi;
+    }
+#pragma unroll
+    for (int k = 0; k < 4; ++k) h[k] = pack_h2(W[2 * k], W[2 * k + 1]);
+    M4[0] = *reinterpret_cast<float4*>(W);
+    M4[1] = *reinterpret_cast<float4*>(W + 4);
+    m4[0] = *reinterpret_cast<float4*>(Mm);
+    m4[1] = *reinterpret_cast<float4*>(Mm + 4);
+    v4[0] = *reinterpret_cast<float4*>(Vv);
+    v4[1] = *reinterpret_cast<float4*>(Vv + 4);
+    *reinterpret_cast<uint4*>(p16) = make_uint4(h[0], h[1], h[2], h[3]);
+}
+
+__global__ void __launch_bounds__(256) k_adam(const OptimArgs a, const AdamScalars* __restrict__ sp, const AdamScalars direct) {
+    const AdamScalars s = sp ? *sp : direct;
+    const uint64_t n_chunks = a.n_params / 8u;
+    const uint64_t grid_chunks = a.n_grid / 8u;
+    uint4* gg = static_cast<uint4*>(a.grid_grad);
+    __half* p16 = static_cast<__half*>(a.params16);
+    for (uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n_chunks;
+         q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        float g[8];
+        if (q < grid_chunks) {
+            const uint4 u = gg[q];
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = unpack_h2(w[k]);
+                g[2 * k] = f.x;
+                g[2 * k + 1] = f.y;
+            }
+            gg[q] = make_uint4(0u, 0u, 0u, 0u);
+        } else {
+            const float4* mg = reinterpret_cast<const float4*>(a.mlp_grad + 8u * (q - grid_chunks));
+            const float4 x = mg[0], y = mg[1];
+            g[0] = x.x; g[1] = x.y; g[2] = x.z; g[3] = x.w;
+            g[4] = y.x; g[5] = y.y; g[6] = y.z; g[7] = y.w;
+        }
+        if (s.skip_update) continue;
+        adam8(a.master + 8u * q, p16 + 8u * q, a.m + 8u * q, a.v + 8u * q, g, s, a.tc.beta1, a.tc.beta2, a.tc.eps);
+    }
+}
+
+__global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, uint64_t n) {
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x)
+        dst[i] = __float2half_rn(src[i]);
+}
+
+uint32_t g_sms = 0;
+uint32_t sm_count() {
+    if (g_sms == 0u) {
+        int dev = 0, sms = 148;
+        if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        g_sms = static_cast<uint32_t>(sms);
+    }
+    return g_sms;
+}
+
+}  // namespace
+
+uint32_t grad_stats_blocks(uint64_t n_params) {
+    const uint64_t chunks = n_params / 8u;
+    const uint64_t want = (chunks + 255u) / 256u;
+    const uint64_t cap = 4ull * sm_count();
+    return static_cast<uint32_t>(want < cap ? (want == 0 ? 1 : want) : cap);
+}
+
+cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s) {
+    k_wgrad_reduce<<<(kMlpParams + 255u) / 256u, 256, 0, s>>>(a.partials, a.n_partials, a.mlp_grad);
+    return cudaGetLastError();
+}
+cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {
+    k_grad_stats<<<a.stats_blocks, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s) {
+    const uint64_t chunks = a.n_params / 8u;
+    uint64_t blocks = (chunks + 255u) / 256u;
+    const uint64_t cap = 8ull * sm_count();
+    if (blocks > cap) blocks = cap;
+    if (blocks == 0u) blocks = 1u;
+    k_adam<<<static_cast<uint32_t>(blocks), 256, 0, s>>>(a, a.state ? &a.state->adam : nullptr, a.direct_scalars);
+    return cudaGetLastError();
+}
+cudaError_t launch_f32_to_f16(const float* src, void* dst, uint64_t n, cudaStream_t s) {
+    if (n == 0u) return cudaSuccess;
+    uint64_t blocks = (n + 255u) / 256u;
+    if (blocks > 4096u) blocks = 4096u;
+    k_f32_to_f16<<<static_cast<uint32_t>(blocks), 256, 0, s>>>(src, static_cast<__half*>(dst), n);
+    return cudaGetLastError();
+}
+
+}  // namespace nb
