@@ -1,7 +1,7 @@
 // composite.cu -- front-to-back volume compositing with the alpha-weighted
-// MSE of the reference and its analytic backward, fused in one pass per ray
+// MSE of the reference and its analytic backward, fused in one kernel
 // (reference backend-cuda.cu:1095-1182; density activation exp instead of
-// softplus, a per-ray background instead of white, and optional early ray
+// softplus, a per-ray background instead of white, optional early ray
 // termination).
 //
 // Per ray with samples i (raw density x_i, raw colour r_i, step dt_i):
@@ -13,18 +13,29 @@
 //   S_i = T_end bg + sum_{j>i} T_j a_j c_j
 //   dL/dx_i = dL/da_i dt_i exp(-sigma_i dt_i) exp(clamp(x_i, -15, 15))
 //   dL/dr_i = T_i a_i g c_i (1 - c_i)
-// Outputs are multiplied by the loss scale.  T_i is parked in dout[i].x by
-// the forward sweep and read back by the backward sweep.
+// Outputs are multiplied by the loss scale.
+//
+// One warp per ray, 32 consecutive samples per chunk (coalesced float4
+// loads).  Forward: T_i from an inclusive product scan of (1 - a) across the
+// warp times the carried transmittance; the early-termination cut is the
+// first lane with T_i < stop (T is non-increasing, so a ballot finds it).
+// T_i is parked in dout[i].x.  Backward: chunks from the last used one down,
+// S_i from a reverse (suffix) sum scan plus the carried suffix of later
+// chunks.  Summation order differs from the sequential CPU oracle, hence the
+// tolerance of the parity test.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace nb {
 namespace {
 
+constexpr uint32_t kWarps = 8;
+
 __device__ __forceinline__ float sigmoidf(float x) { return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x))); }
 
-__global__ void __launch_bounds__(256) k_composite(const CompositeArgs a) {
-    const uint32_t k = blockIdx.x * blockDim.x + threadIdx.x;
+__global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t k = blockIdx.x * kWarps + warp;
     uint32_t n;
     float inv_norm;
     if (a.direct) {
@@ -42,29 +53,53 @@ __global__ void __launch_bounds__(256) k_composite(const CompositeArgs a) {
         float T = 1.0f;
         float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f;
         uint32_t used = count;
-        for (uint32_t i = 0; i < count; ++i) {
-            if (stop > 0.0f && T < stop) {
-                used = i;
+        for (uint32_t base = 0; base < count; base += 32u) {
+            const uint32_t i = base + lane;
+            const bool valid = i < count;
+            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+            float dt = 0.0f;
+            if (valid) {
+                r = a.raw[b + i];
+                dt = fmaxf(0.0f, a.pos_dt[b + i].w);
+            }
+            const float al = valid ? __fsub_rn(1.0f, expf(-__fmul_rn(expf(r.x), dt))) : 0.0f;
+            const float om = __fsub_rn(1.0f, al);
+            float P = om;  // inclusive product of (1 - a) over lanes <= this one
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const float x = __shfl_up_sync(0xffffffffu, P, o);
+                if (lane >= static_cast<uint32_t>(o)) P = __fmul_rn(P, x);
+            }
+            float ex = __shfl_up_sync(0xffffffffu, P, 1);
+            if (lane == 0u) ex = 1.0f;
+            const float Ti = __fmul_rn(T, ex);
+            const bool use = valid && !(stop > 0.0f && Ti < stop);
+            const uint32_t use_mask = __ballot_sync(0xffffffffu, use);
+            if (use) {
+                a.dout[b + i].x = Ti;
+                const float w = __fmul_rn(Ti, al);
+                acc0 = __fmaf_rn(w, sigmoidf(r.y), acc0);
+                acc1 = __fmaf_rn(w, sigmoidf(r.z), acc1);
+                acc2 = __fmaf_rn(w, sigmoidf(r.w), acc2);
+            }
+            const uint32_t n_use = __popc(use_mask);
+            const uint32_t n_valid = min(32u, count - base);
+            if (n_use < n_valid) {  // termination inside this chunk: T_end is T of the first unused sample
+                used = base + n_use;
+                T = __shfl_sync(0xffffffffu, Ti, n_use);
                 break;
             }
-            const float4 r = a.raw[b + i];
-            const float dt = fmaxf(0.0f, a.pos_dt[b + i].w);
-            const float sigma = expf(r.x);
-            const float al = __fsub_rn(1.0f, expf(-__fmul_rn(sigma, dt)));
-            const float w = __fmul_rn(T, al);
-            acc0 = __fadd_rn(acc0, __fmul_rn(w, sigmoidf(r.y)));
-            acc1 = __fadd_rn(acc1, __fmul_rn(w, sigmoidf(r.z)));
-            acc2 = __fadd_rn(acc2, __fmul_rn(w, sigmoidf(r.w)));
-            a.dout[b + i].x = T;
-            T = __fmul_rn(T, __fsub_rn(1.0f, al));
+            T = __fmul_rn(T, __shfl_sync(0xffffffffu, P, 31));
         }
+        acc0 = warp_sum(acc0);
+        acc1 = warp_sum(acc1);
+        acc2 = warp_sum(acc2);
         if (count > 0u) {
             const float ga = fminf(1.0f, fmaxf(0.0f, ray.gt[3]));
             const float ray_w = __fadd_rn(0.1f, __fmul_rn(0.9f, ga));
-            const float p0 = __fadd_rn(acc0, __fmul_rn(T, ray.bg[0]));
-            const float p1 = __fadd_rn(acc1, __fmul_rn(T, ray.bg[1]));
-            const float p2 = __fadd_rn(acc2, __fmul_rn(T, ray.bg[2]));
-            const float d0 = __fsub_rn(p0, ray.gt[0]), d1 = __fsub_rn(p1, ray.gt[1]), d2 = __fsub_rn(p2, ray.gt[2]);
+            const float d0 = __fsub_rn(__fadd_rn(acc0, __fmul_rn(T, ray.bg[0])), ray.gt[0]);
+            const float d1 = __fsub_rn(__fadd_rn(acc1, __fmul_rn(T, ray.bg[1])), ray.gt[1]);
+            const float d2 = __fsub_rn(__fadd_rn(acc2, __fmul_rn(T, ray.bg[2])), ray.gt[2]);
             loss = __fmul_rn(__fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)), __fmul_rn(d2, d2)), ray_w);
             const float two_w = __fmul_rn(2.0f, ray_w);
             const float g0 = __fmul_rn(__fmul_rn(two_w, d0), inv_norm);
@@ -72,45 +107,72 @@ __global__ void __launch_bounds__(256) k_composite(const CompositeArgs a) {
             const float g2 = __fmul_rn(__fmul_rn(two_w, d2), inv_norm);
             float s0 = __fmul_rn(T, ray.bg[0]), s1 = __fmul_rn(T, ray.bg[1]), s2 = __fmul_rn(T, ray.bg[2]);
             const float ls = a.loss_scale;
-            for (int i = static_cast<int>(used) - 1; i >= 0; --i) {
-                const uint32_t s = b + static_cast<uint32_t>(i);
-                const float4 r = a.raw[s];
-                const float dt = fmaxf(0.0f, a.pos_dt[s].w);
-                const float sigma = expf(r.x);
-                const float e = expf(-__fmul_rn(sigma, dt));
-                const float al = __fsub_rn(1.0f, e);
-                const float om = fmaxf(1e-6f, __fsub_rn(1.0f, al));
-                const float trans = a.dout[s].x;
-                const float w = __fmul_rn(trans, al);
-                const float c0 = sigmoidf(r.y), c1 = sigmoidf(r.z), c2 = sigmoidf(r.w);
-                float dL_da = __fmul_rn(g0, __fsub_rn(__fmul_rn(trans, c0), __fdiv_rn(s0, om)));
-                dL_da = __fadd_rn(dL_da, __fmul_rn(g1, __fsub_rn(__fmul_rn(trans, c1), __fdiv_rn(s1, om))));
-                dL_da = __fadd_rn(dL_da, __fmul_rn(g2, __fsub_rn(__fmul_rn(trans, c2), __fdiv_rn(s2, om))));
-                const float xcl = fminf(15.0f, fmaxf(-15.0f, r.x));
-                const float dx = __fmul_rn(__fmul_rn(__fmul_rn(dL_da, dt), e), expf(xcl));
-                float4 o;
-                o.x = __fmul_rn(ls, dx);
-                o.y = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(w, g0), c0), __fsub_rn(1.0f, c0)));
-                o.z = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(w, g1), c1), __fsub_rn(1.0f, c1)));
-                o.w = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(w, g2), c2), __fsub_rn(1.0f, c2)));
-                a.dout[s] = o;
-                s0 = __fadd_rn(s0, __fmul_rn(w, c0));
-                s1 = __fadd_rn(s1, __fmul_rn(w, c1));
-                s2 = __fadd_rn(s2, __fmul_rn(w, c2));
+            if (used > 0u) {
+                for (int base = static_cast<int>((used - 1u) & ~31u); base >= 0; base -= 32) {
+                    const uint32_t i = static_cast<uint32_t>(base) + lane;
+                    const bool valid = i < used;
+                    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
+                    float dt = 0.0f, trans = 0.0f;
+                    if (valid) {
+                        r = a.raw[b + i];
+                        dt = fmaxf(0.0f, a.pos_dt[b + i].w);
+                        trans = a.dout[b + i].x;
+                    }
+                    const float e = expf(-__fmul_rn(expf(r.x), dt));
+                    const float al = __fsub_rn(1.0f, e);
+                    const float om = fmaxf(1e-6f, __fsub_rn(1.0f, al));
+                    const float w = valid ? __fmul_rn(trans, al) : 0.0f;
+                    const float c0 = sigmoidf(r.y), c1 = sigmoidf(r.z), c2 = sigmoidf(r.w);
+                    const float wc0 = __fmul_rn(w, c0), wc1 = __fmul_rn(w, c1), wc2 = __fmul_rn(w, c2);
+                    // inclusive suffix sums over lanes >= this one
+                    float q0 = wc0, q1 = wc1, q2 = wc2;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const float x0 = __shfl_down_sync(0xffffffffu, q0, o);
+                        const float x1 = __shfl_down_sync(0xffffffffu, q1, o);
+                        const float x2 = __shfl_down_sync(0xffffffffu, q2, o);
+                        if (lane + o < 32u) {
+                            q0 = __fadd_rn(q0, x0);
+                            q1 = __fadd_rn(q1, x1);
+                            q2 = __fadd_rn(q2, x2);
+                        }
+                    }
+                    float e0 = __shfl_down_sync(0xffffffffu, q0, 1);
+                    float e1 = __shfl_down_sync(0xffffffffu, q1, 1);
+                    float e2 = __shfl_down_sync(0xffffffffu, q2, 1);
+                    if (lane == 31u) e0 = e1 = e2 = 0.0f;
+                    const float S0 = __fadd_rn(s0, e0), S1 = __fadd_rn(s1, e1), S2 = __fadd_rn(s2, e2);
+                    if (valid) {
+                        float dL_da = __fmul_rn(g0, __fsub_rn(__fmul_rn(trans, c0), __fdiv_rn(S0, om)));
+                        dL_da = __fadd_rn(dL_da, __fmul_rn(g1, __fsub_rn(__fmul_rn(trans, c1), __fdiv_rn(S1, om))));
+                        dL_da = __fadd_rn(dL_da, __fmul_rn(g2, __fsub_rn(__fmul_rn(trans, c2), __fdiv_rn(S2, om))));
+                        const float xcl = fminf(15.0f, fmaxf(-15.0f, r.x));
+                        float4 o;
+                        o.x = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(dL_da, dt), e), expf(xcl)));
+                        o.y = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(w, g0), c0), __fsub_rn(1.0f, c0)));
+                        o.z = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(w, g1), c1), __fsub_rn(1.0f, c1)));
+                        o.w = __fmul_rn(ls, __fmul_rn(__fmul_rn(__fmul_rn(w, g2), c2), __fsub_rn(1.0f, c2)));
+                        a.dout[b + i] = o;
+                    }
+                    s0 = __fadd_rn(s0, __shfl_sync(0xffffffffu, q0, 0));
+                    s1 = __fadd_rn(s1, __shfl_sync(0xffffffffu, q1, 0));
+                    s2 = __fadd_rn(s2, __shfl_sync(0xffffffffu, q2, 0));
+                }
             }
-            for (uint32_t i = used; i < count; ++i) a.dout[b + i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (uint32_t i = used + lane; i < count; i += 32u) a.dout[b + i] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        if (a.ray_loss) a.ray_loss[k] = loss;
-        if (a.ray_used) a.ray_used[k] = used;
+        if (lane == 0u) {
+            if (a.ray_loss) a.ray_loss[k] = loss;
+            if (a.ray_used) a.ray_used[k] = used;
+        }
     }
-    // Block sum of the ray losses, normalised and added to the loss slot.
-    __shared__ float part[8];
-    const float ws = warp_sum(loss);
-    if ((threadIdx.x & 31u) == 0u) part[threadIdx.x >> 5] = ws;
+    // Block sum of the ray losses (lane 0 of each warp holds its ray's), normalised, added to the loss slot.
+    __shared__ float part[kWarps];
+    if (lane == 0u) part[warp] = loss;
     __syncthreads();
     if (threadIdx.x == 0u) {
         float bs = 0.0f;
-        for (uint32_t w = 0; w < blockDim.x / 32u; ++w) bs += part[w];
+        for (uint32_t w = 0; w < kWarps; ++w) bs += part[w];
         if (bs != 0.0f && a.loss_slot) atomicAdd(a.loss_slot, bs * inv_norm);
     }
 }
@@ -120,7 +182,7 @@ __global__ void __launch_bounds__(256) k_composite(const CompositeArgs a) {
 cudaError_t launch_composite(const CompositeArgs& a, cudaStream_t s) {
     const uint32_t rays = a.direct ? a.n_rays : a.max_rays;
     if (rays == 0u) return cudaSuccess;
-    k_composite<<<(rays + 255u) / 256u, 256, 0, s>>>(a);
+    k_composite<<<(rays + kWarps - 1u) / kWarps, kWarps * 32u, 0, s>>>(a);
     return cudaGetLastError();
 }
 

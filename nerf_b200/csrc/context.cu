@@ -215,8 +215,8 @@ struct Context {
     // batch
     uint32_t* ray_counts = nullptr;
     uint32_t* masks = nullptr;
-    uint32_t* block_samples = nullptr;
-    uint32_t* block_active = nullptr;
+    uint32_t* ray_offset = nullptr;
+    uint32_t* ray_slot = nullptr;
     RayRecord* rays = nullptr;
     uint32_t* ray_index = nullptr;
     float4* pos_dt = nullptr;
@@ -467,11 +467,10 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     // batch arena
     n_partials = field_backward_blocks();
     fwd_blocks = field_forward_blocks();
-    const uint32_t sampler_blocks = (t.max_rays + kSamplerBlock - 1u) / kSamplerBlock;
     batch.align = model.align;
     batch.size = 0;
     const uint64_t o_rc = batch.add(t.max_rays * 4ull), o_mask = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
-    const uint64_t o_bs = batch.add(sampler_blocks * 4ull), o_ba = batch.add(sampler_blocks * 4ull);
+    const uint64_t o_bs = batch.add(t.max_rays * 4ull), o_ba = batch.add(t.max_rays * 4ull);
     const uint64_t o_rays = batch.add(t.max_rays * sizeof(RayRecord)), o_ri = batch.add(t.max_rays * 4ull);
     const uint64_t o_pos = batch.add(cap * 16u), o_sr = batch.add(cap * 4u), o_feat = batch.add(cap * 64u);
     const uint64_t o_raw = batch.add(cap * 16u), o_dout = batch.add(cap * 16u);
@@ -480,8 +479,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     if (batch.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
     ray_counts = batch.at<uint32_t>(o_rc);
     masks = batch.at<uint32_t>(o_mask);
-    block_samples = batch.at<uint32_t>(o_bs);
-    block_active = batch.at<uint32_t>(o_ba);
+    ray_offset = batch.at<uint32_t>(o_bs);
+    ray_slot = batch.at<uint32_t>(o_ba);
     rays = batch.at<RayRecord>(o_rays);
     ray_index = batch.at<uint32_t>(o_ri);
     pos_dt = batch.at<float4>(o_pos);
@@ -548,8 +547,8 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     sa.bitfield = bitfield;
     sa.ray_counts = ray_counts;
     sa.masks = masks;
-    sa.block_samples = block_samples;
-    sa.block_active = block_active;
+    sa.ray_offset = ray_offset;
+    sa.ray_slot = ray_slot;
     sa.rays = rays;
     sa.pos_dt = pos_dt;
     sa.sample_ray = sample_ray;

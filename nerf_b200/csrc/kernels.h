@@ -66,14 +66,14 @@ struct SamplerArgs {
     const uint32_t* bitfield;
     uint32_t* ray_counts;     // [max_rays]
     uint32_t* masks;          // [mask_words][max_rays]
-    uint32_t* block_samples;  // [blocks]
-    uint32_t* block_active;   // [blocks]
+    uint32_t* ray_offset;     // [max_rays] exclusive sample prefix
+    uint32_t* ray_slot;       // [max_rays] compacted index, or ~0 when not kept
     RayRecord* rays;          // [max_rays] compacted
     float4* pos_dt;           // [sample_cap]
     uint32_t* sample_ray;     // [sample_cap]
     uint32_t* ray_index;      // [max_rays] compacted -> marched ray index
 };
-constexpr uint32_t kSamplerBlock = 128;
+constexpr uint32_t kSamplerBlock = 256;  // 8 rays (warps) per block
 cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s);
 
 // ---- compositing + loss ----

@@ -143,13 +143,15 @@ __device__ __forceinline__ void adam8(float* master, __half* p16, float* m, floa
     float4* M4 = reinterpret_cast<float4*>(master);
     float4* m4 = reinterpret_cast<float4*>(m);
     float4* v4 = reinterpret_cast<float4*>(v);
+    // Masters and moments are touched once per step: stream them (evict-first)
+    // so that they do not push the hash table out of L2.
     float W[8], Mm[8], Vv[8];
-    *reinterpret_cast<float4*>(W) = M4[0];
-    *reinterpret_cast<float4*>(W + 4) = M4[1];
-    *reinterpret_cast<float4*>(Mm) = m4[0];
-    *reinterpret_cast<float4*>(Mm + 4) = m4[1];
-    *reinterpret_cast<float4*>(Vv) = v4[0];
-    *reinterpret_cast<float4*>(Vv + 4) = v4[1];
+    *reinterpret_cast<float4*>(W) = __ldcs(M4);
+    *reinterpret_cast<float4*>(W + 4) = __ldcs(M4 + 1);
+    *reinterpret_cast<float4*>(Mm) = __ldcs(m4);
+    *reinterpret_cast<float4*>(Mm + 4) = __ldcs(m4 + 1);
+    *reinterpret_cast<float4*>(Vv) = __ldcs(v4);
+    *reinterpret_cast<float4*>(Vv + 4) = __ldcs(v4 + 1);
     const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
     uint32_t h[4];
 #pragma unroll
@@ -166,12 +168,12 @@ __device__ __forceinline__ void adam8(float* master, __half* p16, float* m, floa
     }
 #pragma unroll
     for (int k = 0; k < 4; ++k) h[k] = pack_h2(W[2 * k], W[2 * k + 1]);
-    M4[0] = *reinterpret_cast<float4*>(W);
-    M4[1] = *reinterpret_cast<float4*>(W + 4);
-    m4[0] = *reinterpret_cast<float4*>(Mm);
-    m4[1] = *reinterpret_cast<float4*>(Mm + 4);
-    v4[0] = *reinterpret_cast<float4*>(Vv);
-    v4[1] = *reinterpret_cast<float4*>(Vv + 4);
+    __stcs(M4, *reinterpret_cast<float4*>(W));
+    __stcs(M4 + 1, *reinterpret_cast<float4*>(W + 4));
+    __stcs(m4, *reinterpret_cast<float4*>(Mm));
+    __stcs(m4 + 1, *reinterpret_cast<float4*>(Mm + 4));
+    __stcs(v4, *reinterpret_cast<float4*>(Vv));
+    __stcs(v4 + 1, *reinterpret_cast<float4*>(Vv + 4));
     *reinterpret_cast<uint4*>(p16) = make_uint4(h[0], h[1], h[2], h[3]);
 }
 
@@ -240,9 +242,8 @@ cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {
 }
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s) {
     const uint64_t chunks = a.n_params / 8u;
-    uint64_t blocks = (chunks + 255u) / 256u;
-    const uint64_t cap = 8ull * sm_count();
-    if (blocks > cap) blocks = cap;
+    uint64_t blocks = (chunks + 255u) / 256u;  // one 8-parameter chunk per thread
+    if (blocks > 0x7FFFFFFFull) blocks = 0x7FFFFFFFull;
     if (blocks == 0u) blocks = 1u;
     k_adam<<<static_cast<uint32_t>(blocks), 256, 0, s>>>(a, a.state ? &a.state->adam : nullptr, a.direct_scalars);
     return cudaGetLastError();

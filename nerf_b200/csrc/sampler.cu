@@ -49,34 +49,29 @@ __device__ __forceinline__ bool make_ray(const TrainConsts& tc, const AabbConsts
     return clip_aabb(b, r);
 }
 
-// Block-wide exclusive scan of two counters (128 threads).
-__device__ __forceinline__ void block_scan2(uint32_t a, uint32_t b, uint32_t& ea, uint32_t& eb) {
-    __shared__ uint32_t wa[kSamplerBlock / 32], wb[kSamplerBlock / 32];
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    uint32_t ia = a, ib = b;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t xa = __shfl_up_sync(0xffffffffu, ia, o);
-        const uint32_t xb = __shfl_up_sync(0xffffffffu, ib, o);
-        if (lane >= static_cast<uint32_t>(o)) {
-            ia += xa;
-            ib += xb;
+// The next 32 steps of a ray's march.  Every lane runs the same step
+// recurrence (t is warp-uniform, no divergence) and keeps the step whose
+// index within the chunk equals its lane.  Returns the number of valid steps.
+__device__ __forceinline__ uint32_t march_chunk(const Ray& ray, float dt_min, float cone, uint32_t max_steps, float& t,
+                                                uint32_t& i, uint32_t lane, float& my_mid, float& my_dt) {
+    uint32_t nv = 0u;
+#pragma unroll 4
+    for (uint32_t j = 0; j < 32u; ++j) {
+        if (!(t < ray.tf && i < max_steps)) break;
+        const float dt = march_dt(t, ray.tf, dt_min, cone);
+        if (j == lane) {
+            my_mid = march_mid(t, dt);
+            my_dt = dt;
         }
+        t = __fadd_rn(t, dt);
+        ++i;
+        ++nv;
     }
-    if (lane == 31u) {
-        wa[warp] = ia;
-        wb[warp] = ib;
-    }
-    __syncthreads();
-    uint32_t pa = 0u, pb = 0u;
-    for (uint32_t w = 0; w < warp; ++w) {
-        pa += wa[w];
-        pb += wb[w];
-    }
-    ea = pa + ia - a;
-    eb = pb + ib - b;
+    return nv;
 }
 
+// Pass 1: one warp per ray.  Lane j tests step 32c+j of chunk c; the
+// ballot of the 32 tests is the chunk's bit word.
 __global__ void __launch_bounds__(kSamplerBlock) k_sample_count(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     __shared__ float cam[16];
@@ -84,126 +79,154 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_count(const SamplerArg
     const uint32_t n_rays = a.state->n_rays;
     if (threadIdx.x < 12u) cam[threadIdx.x] = a.cams[16ull * train_camera(frame, tc.n_images) + threadIdx.x];
     __syncthreads();
-    const uint32_t r = blockIdx.x * kSamplerBlock + threadIdx.x;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t r = blockIdx.x * (kSamplerBlock / 32u) + (threadIdx.x >> 5);
+    if (r >= tc.max_rays) return;
     uint32_t count = 0u;
-    if (r < n_rays && r < tc.max_rays) {
+    if (r < n_rays) {
         const AabbConsts box = aabb_of(tc);
         Ray ray;
         float px, py;
         if (make_ray(tc, box, cam, ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r), ray, px, py)) {
             const float dt_min = __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps));
             float t = ray.tn;
-            uint32_t i = 0u, word = 0u;
-            while (t < ray.tf && i < tc.max_steps) {
-                const float dt = march_dt(t, ray.tf, dt_min, tc.cone);
-                float p[3];
-                ray_point(ray, march_mid(t, dt), p);
-                if (occupied(a.bitfield, tc.grid_res, box, p)) {
-                    word |= 1u << (i & 31u);
-                    ++count;
+            uint32_t i = 0u;
+            for (uint32_t c = 0;; ++c) {
+                float mid = 0.0f, dt = 0.0f;
+                const uint32_t nv = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
+                bool occ = false;
+                if (lane < nv) {
+                    float p[3];
+                    ray_point(ray, mid, p);
+                    occ = occupied(a.bitfield, tc.grid_res, box, p);
                 }
-                if ((i & 31u) == 31u) {
-                    a.masks[(i >> 5) * tc.max_rays + r] = word;
-                    word = 0u;
-                }
-                t = __fadd_rn(t, dt);
-                ++i;
+                const uint32_t bits = __ballot_sync(0xffffffffu, occ);
+                if (nv > 0u && lane == 0u) a.masks[c * tc.max_rays + r] = bits;
+                count += __popc(bits);
+                if (nv < 32u) break;
             }
-            if ((i & 31u) != 0u) a.masks[(i >> 5) * tc.max_rays + r] = word;
         }
     }
-    if (r < tc.max_rays) a.ray_counts[r] = count;
-    const uint32_t s = warp_sum_u32(count), act = warp_sum_u32(count > 0u ? 1u : 0u);
-    __shared__ uint32_t ws[kSamplerBlock / 32], wa[kSamplerBlock / 32];
-    if ((threadIdx.x & 31u) == 0u) {
-        ws[threadIdx.x >> 5] = s;
-        wa[threadIdx.x >> 5] = act;
+    if (lane == 0u) a.ray_counts[r] = count;
+}
+
+// Ordered compaction over all marched rays in one block: exclusive scans of
+// sample counts and of the active flags; a ray is kept while its inclusive
+// sample prefix stays within the capacity (kept rays are a prefix of the
+// active rays, so a kept ray's slot is its active index).
+constexpr uint32_t kScanThreads = 1024;
+__global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs a) {
+    const TrainConsts& tc = a.tc;
+    const uint32_t n = min(a.state->n_rays, tc.max_rays);
+    const uint32_t per = (n + kScanThreads - 1u) / kScanThreads;
+    const uint32_t r0 = threadIdx.x * per, r1 = min(n, r0 + per);
+    uint32_t ls = 0u, la = 0u;
+    for (uint32_t r = r0; r < r1; ++r) {
+        const uint32_t c = a.ray_counts[r];
+        ls += c;
+        la += c > 0u ? 1u : 0u;
+    }
+    __shared__ uint32_t ws[32], wa[32];
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    uint32_t is = ls, ia = la;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t xs = __shfl_up_sync(0xffffffffu, is, o), xa = __shfl_up_sync(0xffffffffu, ia, o);
+        if (lane >= static_cast<uint32_t>(o)) {
+            is += xs;
+            ia += xa;
+        }
+    }
+    if (lane == 31u) {
+        ws[warp] = is;
+        wa[warp] = ia;
     }
     __syncthreads();
-    if (threadIdx.x == 0u) {
-        uint32_t bs = 0u, ba = 0u;
-        for (uint32_t w = 0; w < kSamplerBlock / 32; ++w) {
-            bs += ws[w];
-            ba += wa[w];
+    if (warp == 0u) {
+        uint32_t vs = ws[lane], va = wa[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t xs = __shfl_up_sync(0xffffffffu, vs, o), xa = __shfl_up_sync(0xffffffffu, va, o);
+            if (lane >= static_cast<uint32_t>(o)) {
+                vs += xs;
+                va += xa;
+            }
         }
-        a.block_samples[blockIdx.x] = bs;
-        a.block_active[blockIdx.x] = ba;
+        ws[lane] = vs;  // inclusive over warps
+        wa[lane] = va;
+    }
+    __syncthreads();
+    uint32_t ps = is - ls + (warp ? ws[warp - 1u] : 0u);
+    uint32_t pa = ia - la + (warp ? wa[warp - 1u] : 0u);
+    const uint32_t tot_s = ws[31], tot_a = wa[31];
+    const uint32_t cap = tc.sample_cap;
+    for (uint32_t r = r0; r < r1; ++r) {
+        const uint32_t c = a.ray_counts[r];
+        const uint32_t incl = ps + c;
+        const bool kept = c > 0u && incl <= cap;
+        a.ray_offset[r] = ps;
+        a.ray_slot[r] = kept ? pa : 0xFFFFFFFFu;
+        if (c > 0u && ps <= cap && incl > cap) {  // the first ray past the capacity
+            a.state->n_samples = ps;
+            a.state->n_active = pa;
+        }
+        ps = incl;
+        pa += c > 0u ? 1u : 0u;
+    }
+    if (threadIdx.x == 0u) {
+        a.state->n_marched_active = tot_a;
+        if (tot_s <= cap) {
+            a.state->n_samples = tot_s;
+            a.state->n_active = tot_a;
+        }
     }
 }
 
+// Pass 2: one warp per kept ray.  The same step recurrence is re-walked; the
+// pass-1 bit words say which steps are samples, and lane j writes step
+// 32c+j at its rank among the chunk's set bits.
 __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     __shared__ float cam[16];
-    __shared__ uint32_t pre_s, pre_a, tot_s, tot_a;
     const uint32_t frame = a.state->frame_index;
     const uint32_t camera = train_camera(frame, tc.n_images);
     if (threadIdx.x < 12u) cam[threadIdx.x] = a.cams[16ull * camera + threadIdx.x];
-    if (threadIdx.x < 32u) {
-        uint32_t ps = 0u, pa = 0u, ts = 0u, ta = 0u;
-        for (uint32_t j = threadIdx.x; j < gridDim.x; j += 32u) {
-            const uint32_t bs = a.block_samples[j], ba = a.block_active[j];
-            ts += bs;
-            ta += ba;
-            if (j < blockIdx.x) {
-                ps += bs;
-                pa += ba;
-            }
-        }
-        ps = warp_sum_u32(ps);
-        pa = warp_sum_u32(pa);
-        ts = warp_sum_u32(ts);
-        ta = warp_sum_u32(ta);
-        if (threadIdx.x == 0u) {
-            pre_s = ps;
-            pre_a = pa;
-            tot_s = ts;
-            tot_a = ta;
-        }
-    }
-    const uint32_t r = blockIdx.x * kSamplerBlock + threadIdx.x;
-    const uint32_t count = r < tc.max_rays ? a.ray_counts[r] : 0u;
-    uint32_t ex_s, ex_a;
-    block_scan2(count, count > 0u ? 1u : 0u, ex_s, ex_a);  // contains __syncthreads
-    const uint32_t excl = pre_s + ex_s, incl = excl + count;
-    const uint32_t slot = pre_a + ex_a;
-    const uint32_t cap = tc.sample_cap;
-    if (tot_s <= cap) {
-        if (blockIdx.x == 0u && threadIdx.x == 0u) {
-            a.state->n_samples = tot_s;
-            a.state->n_active = tot_a;
-            a.state->n_marched_active = tot_a;
-        }
-    } else if (count > 0u && excl <= cap && incl > cap) {
-        a.state->n_samples = excl;
-        a.state->n_active = slot;
-        a.state->n_marched_active = tot_a;
-    }
-    if (count == 0u || incl > cap) return;
+    __syncthreads();
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t r = blockIdx.x * (kSamplerBlock / 32u) + (threadIdx.x >> 5);
+    if (r >= min(a.state->n_rays, tc.max_rays)) return;
+    const uint32_t count = a.ray_counts[r];
+    if (count == 0u) return;
+    const uint32_t slot = a.ray_slot[r];
+    if (slot == 0xFFFFFFFFu) return;
+    const uint32_t excl = a.ray_offset[r];
 
     const AabbConsts box = aabb_of(tc);
     Ray ray;
     float rpx = 0.0f, rpy = 0.0f;
-    const uint32_t gr = tc.dp_rank * tc.rays_per_batch + r;
-    const uint32_t seed = ray_seed(frame, gr);
+    const uint32_t seed = ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r);
     make_ray(tc, box, cam, seed, ray, rpx, rpy);
-    a.ray_index[slot] = r;
-    // Re-walk the step recurrence; the pass-1 bits say which steps to keep.
     const float dt_min = __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps));
     float t = ray.tn;
-    uint32_t i = 0u, out = excl, word = 0u;
-    while (t < ray.tf && i < tc.max_steps && out < incl) {
-        if ((i & 31u) == 0u) word = a.masks[(i >> 5) * tc.max_rays + r];
-        const float dt = march_dt(t, ray.tf, dt_min, tc.cone);
-        if ((word >> (i & 31u)) & 1u) {
+    uint32_t i = 0u, out = excl;
+    const uint32_t end = excl + count;
+    for (uint32_t c = 0; out < end; ++c) {
+        float mid = 0.0f, dt = 0.0f;
+        const uint32_t nv = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
+        if (nv == 0u) break;
+        const uint32_t bits = a.masks[c * tc.max_rays + r];
+        if ((bits >> lane) & 1u) {
             float p[3];
-            ray_point(ray, march_mid(t, dt), p);
-            a.pos_dt[out] = make_float4(p[0], p[1], p[2], dt);
-            a.sample_ray[out] = slot;
-            ++out;
+            ray_point(ray, mid, p);
+            const uint32_t o = out + __popc(bits & ((1u << lane) - 1u));
+            a.pos_dt[o] = make_float4(p[0], p[1], p[2], dt);
+            a.sample_ray[o] = slot;
         }
-        t = __fadd_rn(t, dt);
-        ++i;
+        out += __popc(bits);
+        if (nv < 32u) break;
     }
+    if (lane != 0u) return;
+    a.ray_index[slot] = r;
     // Ground truth: bilinear RGBA8 fetch at the unflipped pixel position,
     // composited on the ray's background (reference backend-cuda.cu:471-499).
     float bg[3] = {1.0f, 1.0f, 1.0f};
@@ -254,10 +277,13 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
 }  // namespace
 
 cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s) {
-    const uint32_t blocks = (a.tc.max_rays + kSamplerBlock - 1u) / kSamplerBlock;
+    const uint32_t rays_per_block = kSamplerBlock / 32u;
+    const uint32_t blocks = (a.tc.max_rays + rays_per_block - 1u) / rays_per_block;
     k_sample_count<<<blocks, kSamplerBlock, 0, s>>>(a);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    k_sample_scan<<<1, kScanThreads, 0, s>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_sample_write<<<blocks, kSamplerBlock, 0, s>>>(a);
     return cudaGetLastError();
 }
