@@ -8,8 +8,10 @@ spheres/boxes with value-noise albedo in [-1.5,1.5]^3, 100 training views at
 hash grid L16 F2 T=2^19 N_max=2048; <= 1024 steps per ray; 2^18 target
 compacted samples per step per GPU; 128^3 occupancy refreshed every 16 steps;
 random background; Adam lr 1e-2, betas 0.9/0.99, eps 1e-15.  One "step" is
-one nerf_train_step.  The timed steps run after an untimed pretrain past the
-occupancy warm-up, so they measure steady-state training.
+one nerf_train_step.  The timed steps run after an untimed pretrain of 2000
+steps: past the occupancy warm-up and the ~1440 steps the decayed warm-up
+densities need to fall below the threshold, so empty space is pruned and the
+steps measure steady-state training.
 
 value: compacted samples trained per second over all ranks (device time, CUDA
 events on each context's stream, max over ranks).  e2e: the same metric for
@@ -440,7 +442,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--pretrain", type=int, default=400)
+    ap.add_argument("--pretrain", type=int, default=2000)
     ap.add_argument("--profile-steps", type=int, default=20)
     ap.add_argument("--render-views", type=int, default=20)
     ap.add_argument("--e2e-steps", type=int, default=1000)

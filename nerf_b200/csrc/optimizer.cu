@@ -10,7 +10,7 @@
 //                   backend-cuda.cu:1451-1536: grad stats, finalize, Adam
 //                   scalars and commit, folded into one launch).
 //   k_adam          Adam on fp32 masters with the fp16 mirror, one pass over
-//                   the flat parameter vector, 8 parameters per thread; the
+//                   the flat parameter vector, 4 parameters per thread; the
 //                   hash-table gradients are cleared behind it for the next
 //                   step (reference backend-cuda.cu:1537-1554).
 #include "common.cuh"
@@ -137,74 +137,62 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     a.mlp_grad[kMlpGradLoss] = 0.0f;
 }
 
-// Adam for 8 consecutive parameters; g holds the loss-scaled gradients.
-__device__ __forceinline__ void adam8(float* master, __half* p16, float* m, float* v, const float g[8], const AdamScalars& s,
+// Adam for 4 consecutive parameters; g holds the loss-scaled gradients.
+// Masters and moments are touched once per step: they are streamed
+// (evict-first) so that they do not push the hash table out of L2.
+__device__ __forceinline__ void adam4(float* master, __half* p16, float* m, float* v, const float g[4], const AdamScalars& s,
                                       float b1, float b2, float eps) {
     float4* M4 = reinterpret_cast<float4*>(master);
     float4* m4 = reinterpret_cast<float4*>(m);
     float4* v4 = reinterpret_cast<float4*>(v);
-    // Masters and moments are touched once per step: stream them (evict-first)
-    // so that they do not push the hash table out of L2.
-    float W[8], Mm[8], Vv[8];
-    *reinterpret_cast<float4*>(W) = __ldcs(M4);
-    *reinterpret_cast<float4*>(W + 4) = __ldcs(M4 + 1);
-    *reinterpret_cast<float4*>(Mm) = __ldcs(m4);
-    *reinterpret_cast<float4*>(Mm + 4) = __ldcs(m4 + 1);
-    *reinterpret_cast<float4*>(Vv) = __ldcs(v4);
-    *reinterpret_cast<float4*>(Vv + 4) = __ldcs(v4 + 1);
+    float4 W = __ldcs(M4), Mm = __ldcs(m4), Vv = __ldcs(v4);
+    float* w = reinterpret_cast<float*>(&W);
+    float* mm = reinterpret_cast<float*>(&Mm);
+    float* vv = reinterpret_cast<float*>(&Vv);
     const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
-    uint32_t h[4];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < 4; ++k) {
         const float gk = __fmul_rn(__fmul_rn(g[k], s.inv_loss_scale), s.grad_scale);
-        const float mi = __fadd_rn(__fmul_rn(b1, Mm[k]), __fmul_rn(omb1, gk));
-        const float vi = __fadd_rn(__fmul_rn(b2, Vv[k]), __fmul_rn(__fmul_rn(omb2, gk), gk));
+        const float mi = __fadd_rn(__fmul_rn(b1, mm[k]), __fmul_rn(omb1, gk));
+        const float vi = __fadd_rn(__fmul_rn(b2, vv[k]), __fmul_rn(__fmul_rn(omb2, gk), gk));
         const float num = __fmul_rn(s.learning_rate, __fmul_rn(mi, s.inv_bias_correction1));
         const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vi, s.inv_bias_correction2)), eps);
-        const float w = __fsub_rn(W[k], __fdiv_rn(num, den));
-        W[k] = w;
-        Mm[k] = mi;
-        Vv[k] = vi;
+        w[k] = __fsub_rn(w[k], __fdiv_rn(num, den));
+        mm[k] = mi;
+        vv[k] = vi;
     }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) h[k] = pack_h2(W[2 * k], W[2 * k + 1]);
-    __stcs(M4, *reinterpret_cast<float4*>(W));
-    __stcs(M4 + 1, *reinterpret_cast<float4*>(W + 4));
-    __stcs(m4, *reinterpret_cast<float4*>(Mm));
-    __stcs(m4 + 1, *reinterpret_cast<float4*>(Mm + 4));
-    __stcs(v4, *reinterpret_cast<float4*>(Vv));
-    __stcs(v4 + 1, *reinterpret_cast<float4*>(Vv + 4));
-    *reinterpret_cast<uint4*>(p16) = make_uint4(h[0], h[1], h[2], h[3]);
+    __stcs(M4, W);
+    __stcs(m4, Mm);
+    __stcs(v4, Vv);
+    *reinterpret_cast<uint2*>(p16) = make_uint2(pack_h2(w[0], w[1]), pack_h2(w[2], w[3]));
 }
 
+// One 4-parameter chunk per thread over the flat vector (hash part first).
 __global__ void __launch_bounds__(256) k_adam(const OptimArgs a, const AdamScalars* __restrict__ sp, const AdamScalars direct) {
+    const uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (q >= a.n_params / 4u) return;
     const AdamScalars s = sp ? *sp : direct;
-    const uint64_t n_chunks = a.n_params / 8u;
-    const uint64_t grid_chunks = a.n_grid / 8u;
-    uint4* gg = static_cast<uint4*>(a.grid_grad);
-    __half* p16 = static_cast<__half*>(a.params16);
-    for (uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n_chunks;
-         q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-        float g[8];
-        if (q < grid_chunks) {
-            const uint4 u = gg[q];
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float2 f = unpack_h2(w[k]);
-                g[2 * k] = f.x;
-                g[2 * k + 1] = f.y;
-            }
-            gg[q] = make_uint4(0u, 0u, 0u, 0u);
-        } else {
-            const float4* mg = reinterpret_cast<const float4*>(a.mlp_grad + 8u * (q - grid_chunks));
-            const float4 x = mg[0], y = mg[1];
-            g[0] = x.x; g[1] = x.y; g[2] = x.z; g[3] = x.w;
-            g[4] = y.x; g[5] = y.y; g[6] = y.z; g[7] = y.w;
-        }
-        if (s.skip_update) continue;
-        adam8(a.master + 8u * q, p16 + 8u * q, a.m + 8u * q, a.v + 8u * q, g, s, a.tc.beta1, a.tc.beta2, a.tc.eps);
+    const uint64_t grid_chunks = a.n_grid / 4u;
+    float g[4];
+    if (q < grid_chunks) {
+        uint2* gg = static_cast<uint2*>(a.grid_grad) + q;
+        const uint2 u = *gg;
+        const float2 f0 = unpack_h2(u.x), f1 = unpack_h2(u.y);
+        g[0] = f0.x;
+        g[1] = f0.y;
+        g[2] = f1.x;
+        g[3] = f1.y;
+        *gg = make_uint2(0u, 0u);  // cleared for the next step's reductions
+    } else {
+        const float4 x = reinterpret_cast<const float4*>(a.mlp_grad)[q - grid_chunks];
+        g[0] = x.x;
+        g[1] = x.y;
+        g[2] = x.z;
+        g[3] = x.w;
     }
+    if (s.skip_update) return;
+    adam4(a.master + 4u * q, static_cast<__half*>(a.params16) + 4u * q, a.m + 4u * q, a.v + 4u * q, g, s, a.tc.beta1,
+          a.tc.beta2, a.tc.eps);
 }
 
 __global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, uint64_t n) {
@@ -241,8 +229,8 @@ cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s) {
-    const uint64_t chunks = a.n_params / 8u;
-    uint64_t blocks = (chunks + 255u) / 256u;  // one 8-parameter chunk per thread
+    const uint64_t chunks = a.n_params / 4u;
+    uint64_t blocks = (chunks + 255u) / 256u;  // one 4-parameter chunk per thread
     if (blocks > 0x7FFFFFFFull) blocks = 0x7FFFFFFFull;
     if (blocks == 0u) blocks = 1u;
     k_adam<<<static_cast<uint32_t>(blocks), 256, 0, s>>>(a, a.state ? &a.state->adam : nullptr, a.direct_scalars);
