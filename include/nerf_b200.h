@@ -206,6 +206,23 @@ NERF_API uint64_t nerf_b200_field_backward_partial_floats(void);
 NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, const void* params_f16, const float* pos_unit,
                                              const float* dirs, uint32_t n, const void* feat_f16, const float* dout,
                                              void* grid_grad_f16, float* partials, float* mlp_grad, void* stream);
+/* Allocation-free nerf_b200_field_backward (no counterpart in the reference).
+ * For callers that cannot allocate device memory -- a plugin inside a host
+ * application that owns the device memory budget, or code where a cudaMalloc
+ * would synchronise the device at the wrong moment.  The weight-gradient
+ * scratch lives in a static device array of
+ * nerf_b200_field_backward_noalloc_max_rows() x 10240 floats (13.1 MB, held
+ * by every GPU that loads the library until exit); the call fails with
+ * NERF_STATUS_INVALID_USAGE when this GPU needs more rows (more than 160
+ * SMs) or n exceeds 2^31-1.  The first call on a device looks up the array's
+ * device address; make it before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race.  Other arguments as in
+ * nerf_b200_field_backward. */
+NERF_API uint32_t nerf_b200_field_backward_noalloc_max_rows(void);
+NERF_API NerfStatus nerf_b200_field_backward_noalloc(const NerfB200GridLayout* layout, const void* params_f16,
+                                                     const float* pos_unit, const float* dirs, uint32_t n,
+                                                     const void* feat_f16, const float* dout, void* grid_grad_f16,
+                                                     float* mlp_grad, void* stream);
 /* Compositing + alpha-weighted MSE forward and backward over n_rays rays
  * (ray records as in nerf_b200_read_batch), raw (S x 4), pos_dt (S x 4, only
  * .w = dt is read).  Writes loss_scale * dL/draw to dout, per-ray loss and
