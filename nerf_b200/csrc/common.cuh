@@ -113,6 +113,24 @@ NB_DEV void load_b_kn(uint32_t b[4], const __half* base, uint32_t stride, uint32
 }
 
 // ---------------------------------------------------------------------------
+// Asynchronous global -> shared copies (cp.async); a copy with valid == false
+// reads nothing and zero-fills its destination.
+// ---------------------------------------------------------------------------
+NB_DEV void cp_async16(void* smem, const void* gmem, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+NB_DEV void cp_async4(void* smem, const void* gmem, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(valid ? 4 : 0)
+                 : "memory");
+}
+NB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+NB_DEV void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// ---------------------------------------------------------------------------
 // Global atomics
 // ---------------------------------------------------------------------------
 // Adds a packed f16x2 to global memory at L2 without returning the old value.

@@ -39,10 +39,6 @@ constexpr uint32_t kWC1 = kWC0 + 64 * kS32;   // 64 x 64
 constexpr uint32_t kWC2 = kWC1 + 64 * kS64;   // 16 x 64
 constexpr uint32_t kWTotal = kWC2 + 16 * kS64;
 
-// Forward shared memory: weights | feat[64][40] | xc[64][40] | pos[64] float4 | levels
-constexpr size_t kFwdSmem = (kWTotal + 2 * kRows * kS32) * 2 + kRows * 16 + kMaxLevels * 16;
-// Backward adds hd, dhd, h1, dh1, h2, dh2 [64][72] and dyd, dyc [64][24].
-constexpr size_t kBwdSmem = kFwdSmem + (6 * kRows * kS64 + 2 * kRows * kS16) * 2;
 
 __device__ __forceinline__ void copy_matrix(__half* dst, uint32_t stride, const __half* src, uint32_t rows, uint32_t cols) {
     const uint32_t q = cols / 8u;
@@ -150,34 +146,86 @@ __device__ __forceinline__ void store_a(__half* base, uint32_t stride, uint32_t 
     *reinterpret_cast<uint32_t*>(base + (row0 + g + 8u) * stride + kc * 16u + 8u + 2u * t) = a[3];
 }
 
+// Shared memory of the forward kernel and the renderer (the renderer appends
+// its slots after kFwdBase): weights | feat[64][40] | xc[64][40] | pos[64]
+// (unit position) | levels.  The training forward appends two stages of the
+// next tile's raw inputs (pos+dt, ray id), filled with cp.async.
 struct Smem {
     __half* w;
     __half* feat;
     __half* xc;
     float4* pos;
     LevelParams* lv;
-    // backward only
-    __half *hd, *dhd, *h1, *dh1, *h2, *dh2, *dyd, *dyc;
 };
-__device__ __forceinline__ Smem carve(unsigned char* raw, bool backward) {
+constexpr size_t kFwdBase = (kWTotal + 2 * kRows * kS32) * 2 + kRows * 16 + kMaxLevels * 16;
+constexpr size_t kFwdStage = kRows * 16 + kRows * 4;
+constexpr size_t kFwdSmem = kFwdBase + 2 * kFwdStage;
+
+__device__ __forceinline__ Smem carve(unsigned char* raw) {
     Smem s{};
     s.w = reinterpret_cast<__half*>(raw);
     s.feat = s.w + kWTotal;
     s.xc = s.feat + kRows * kS32;
     s.pos = reinterpret_cast<float4*>(s.xc + kRows * kS32);
     s.lv = reinterpret_cast<LevelParams*>(s.pos + kRows);
-    if (backward) {
-        __half* b = reinterpret_cast<__half*>(s.lv + kMaxLevels);
-        s.hd = b;
-        s.dhd = s.hd + kRows * kS64;
-        s.h1 = s.dhd + kRows * kS64;
-        s.dh1 = s.h1 + kRows * kS64;
-        s.h2 = s.dh1 + kRows * kS64;
-        s.dh2 = s.h2 + kRows * kS64;
-        s.dyd = s.dh2 + kRows * kS64;
-        s.dyc = s.dyd + kRows * kS16;
-    }
     return s;
+}
+struct FwdStage {
+    float4* pos;     // raw pos_dt of the tile
+    uint32_t* sray;  // ray id of each row
+};
+__device__ __forceinline__ FwdStage fwd_stage(unsigned char* raw, uint32_t k) {
+    FwdStage st;
+    st.pos = reinterpret_cast<float4*>(raw + kFwdBase + k * kFwdStage);
+    st.sray = reinterpret_cast<uint32_t*>(st.pos + kRows);
+    return st;
+}
+
+// Shared memory of the backward kernel: weights | xc[64][40] | levels |
+// activation staging for the weight gradients (hd, dhd, h1, dh1, h2, dh2
+// [64][72]; dyd, dyc [64][24]) | two input stages (features [64][40], pos+dt,
+// upstream gradient, ray id, direction), filled with cp.async one tile ahead.
+struct BwdSmem {
+    __half* w;
+    __half* xc;
+    LevelParams* lv;
+    __half *hd, *dhd, *h1, *dh1, *h2, *dh2, *dyd, *dyc;
+};
+struct BwdStage {
+    __half* feat;
+    float4* pos;
+    float4* dout;
+    float4* dir;
+    uint32_t* sray;
+};
+constexpr size_t kBwdFixed = kWTotal * 2 + kRows * kS32 * 2 + kMaxLevels * 16 + (6 * kRows * kS64 + 2 * kRows * kS16) * 2;
+constexpr size_t kBwdStage = kRows * kS32 * 2 + 3 * kRows * 16 + kRows * 4;
+constexpr size_t kBwdSmem = kBwdFixed + 2 * kBwdStage;
+
+__device__ __forceinline__ BwdSmem carve_bwd(unsigned char* raw) {
+    BwdSmem s{};
+    s.w = reinterpret_cast<__half*>(raw);
+    s.xc = s.w + kWTotal;
+    s.lv = reinterpret_cast<LevelParams*>(s.xc + kRows * kS32);
+    __half* b = reinterpret_cast<__half*>(s.lv + kMaxLevels);
+    s.hd = b;
+    s.dhd = s.hd + kRows * kS64;
+    s.h1 = s.dhd + kRows * kS64;
+    s.dh1 = s.h1 + kRows * kS64;
+    s.h2 = s.dh1 + kRows * kS64;
+    s.dh2 = s.h2 + kRows * kS64;
+    s.dyd = s.dh2 + kRows * kS64;
+    s.dyc = s.dyd + kRows * kS16;
+    return s;
+}
+__device__ __forceinline__ BwdStage bwd_stage(unsigned char* raw, uint32_t k) {
+    BwdStage st;
+    st.feat = reinterpret_cast<__half*>(raw + kBwdFixed + k * kBwdStage);
+    st.pos = reinterpret_cast<float4*>(st.feat + kRows * kS32);
+    st.dout = st.pos + kRows;
+    st.dir = st.dout + kRows;
+    st.sray = reinterpret_cast<uint32_t*>(st.dir + kRows);
+    return st;
 }
 
 __device__ __forceinline__ uint32_t row_count(const FieldArgs& a, int mode) {
@@ -189,19 +237,51 @@ __device__ __forceinline__ uint32_t row_count(const FieldArgs& a, int mode) {
     return a.n_direct;
 }
 
+__device__ __forceinline__ void world_to_unit(const FieldArgs& a, const float pw[3], float u[3]) {
+#pragma unroll
+    for (int k = 0; k < 3; ++k) u[k] = clamp01(__fdiv_rn(__fsub_rn(pw[k], a.aabb_min[k]), a.aabb_size[k]));
+}
+
+__device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool valid) {
+    float sh[16];
+    if (valid) {
+        sh4(d[0], d[1], d[2], sh);
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) sh[k] = 0.0f;
+    }
+    uint32_t* dst = reinterpret_cast<uint32_t*>(xc_row + 16u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) dst[k] = pack_h2(sh[2 * k], sh[2 * k + 1]);
+}
+
+// Training forward: copies of the next tile's pos+dt and ray ids.
+__device__ __forceinline__ void fwd_prefetch(const FieldArgs& a, const FwdStage& st, uint32_t row0, uint32_t n) {
+    const uint32_t tid = threadIdx.x;
+    if (tid < kRows) {
+        const uint32_t r = row0 + tid;
+        cp_async16(st.pos + tid, a.pos_dt + (r < n ? r : 0u), r < n);
+    } else {
+        const uint32_t i = tid - kRows;
+        const uint32_t r = row0 + i;
+        cp_async4(st.sray + i, a.sample_ray + (r < n ? r : 0u), r < n);
+    }
+}
+
 // Per-row inputs of a tile: unit position -> s.pos, SH(dir) -> s.xc[:,16:32].
-__device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Smem& s, uint32_t row0, uint32_t n) {
+__device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Smem& s, const FwdStage* st, uint32_t row0,
+                                          uint32_t n) {
     const uint32_t tid = threadIdx.x;
     if (tid >= kRows) return;
     const uint32_t r = row0 + tid;
     float u[3] = {0.0f, 0.0f, 0.0f}, d[3] = {0.0f, 0.0f, 0.0f};
-    if (r < n) {
+    const bool valid = r < n;
+    if (valid) {
         if (mode == kFieldTrain) {
-            const float4 p = a.pos_dt[r];
+            const float4 p = st->pos[tid];
             const float pw[3] = {p.x, p.y, p.z};
-#pragma unroll
-            for (int k = 0; k < 3; ++k) u[k] = clamp01(__fdiv_rn(__fsub_rn(pw[k], a.aabb_min[k]), a.aabb_size[k]));
-            const RayRecord& ray = a.rays[a.sample_ray[r]];
+            world_to_unit(a, pw, u);
+            const RayRecord& ray = a.rays[st->sray[tid]];
             d[0] = ray.dir[0];
             d[1] = ray.dir[1];
             d[2] = ray.dir[2];
@@ -212,12 +292,13 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
             const uint32_t cell = static_cast<uint32_t>((static_cast<unsigned long long>(start) + r) % a.cell_count);
             const uint32_t z = cell / (R * R), rem = cell - z * R * R, y = rem / R, x = rem - y * R;
             const uint32_t ci[3] = {x, y, z};
+            float c[3];
 #pragma unroll
             for (int k = 0; k < 3; ++k) {
                 const float step = __fdiv_rn(__fsub_rn(a.aabb_max[k], a.aabb_min[k]), static_cast<float>(R));
-                const float c = __fmaf_rn(__fadd_rn(static_cast<float>(ci[k]), 0.5f), step, a.aabb_min[k]);
-                u[k] = clamp01(__fdiv_rn(__fsub_rn(c, a.aabb_min[k]), a.aabb_size[k]));
+                c[k] = __fmaf_rn(__fadd_rn(static_cast<float>(ci[k]), 0.5f), step, a.aabb_min[k]);
             }
+            world_to_unit(a, c, u);
         } else {
 #pragma unroll
             for (int k = 0; k < 3; ++k) {
@@ -227,16 +308,7 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
         }
     }
     s.pos[tid] = make_float4(u[0], u[1], u[2], 0.0f);
-    float sh[16];
-    if (r < n && mode != kFieldOccupancy) {
-        sh4(d[0], d[1], d[2], sh);
-    } else {
-#pragma unroll
-        for (int k = 0; k < 16; ++k) sh[k] = 0.0f;
-    }
-    uint32_t* dst = reinterpret_cast<uint32_t*>(s.xc + tid * kS32 + 16u);
-#pragma unroll
-    for (int k = 0; k < 8; ++k) dst[k] = pack_h2(sh[2 * k], sh[2 * k + 1]);
+    write_sh(s.xc + tid * kS32, d, valid && mode != kFieldOccupancy);
 }
 
 // Hash-grid encode of a tile: 64 rows x 16 levels over 128 threads; each
@@ -270,21 +342,10 @@ __device__ __forceinline__ void encode_tile(const FieldArgs& a, const Smem& s, u
     }
 }
 
-// Stored hash features of a tile (backward): 64 rows x 64 B.
-__device__ __forceinline__ void load_feat_tile(const FieldArgs& a, const Smem& s, uint32_t row0, uint32_t n) {
-    const uint4* src = static_cast<const uint4*>(a.feat);
-    for (uint32_t c = threadIdx.x; c < kRows * 4u; c += kThreads) {
-        const uint32_t r = c / 4u, q = c % 4u;
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (row0 + r < n) v = src[static_cast<unsigned long long>(row0 + r) * 4u + q];
-        *reinterpret_cast<uint4*>(s.feat + r * kS32 + q * 8u) = v;
-    }
-}
-
-__device__ __forceinline__ void load_levels(const FieldArgs& a, const Smem& s) {
-    if (threadIdx.x < a.lt.n_levels) {
+__device__ __forceinline__ void load_levels(const LevelTable& lt, LevelParams* lv) {
+    if (threadIdx.x < lt.n_levels) {
         const uint32_t l = threadIdx.x;
-        s.lv[l] = LevelParams{a.lt.scale[l], a.lt.res[l], a.lt.dense[l], a.lt.offset[l]};
+        lv[l] = LevelParams{lt.scale[l], lt.res[l], lt.dense[l], lt.offset[l]};
     }
 }
 
@@ -298,49 +359,57 @@ struct Chain {
     uint32_t h2[4][4];
     float yc[2][4];
 };
-__device__ __forceinline__ void forward_density(const Smem& s, uint32_t wrow, uint32_t lane, Chain& c) {
-    load_a_rowmajor(c.xd[0], s.feat, kS32, wrow, 0, lane);
-    load_a_rowmajor(c.xd[1], s.feat, kS32, wrow, 16, lane);
+__device__ __forceinline__ void forward_density(const __half* w, const __half* feat, uint32_t wrow, uint32_t lane, Chain& c) {
+    load_a_rowmajor(c.xd[0], feat, kS32, wrow, 0, lane);
+    load_a_rowmajor(c.xd[1], feat, kS32, wrow, 16, lane);
     float acc[8][4];
-    gemm_nk<8, 2>(acc, c.xd, s.w + kWD0, kS32, lane);
+    gemm_nk<8, 2>(acc, c.xd, w + kWD0, kS32, lane);
     relu_to_a<8>(acc, c.hd);
-    gemm_nk<2, 4>(c.yd, c.hd, s.w + kWD1, kS64, lane);
+    gemm_nk<2, 4>(c.yd, c.hd, w + kWD1, kS64, lane);
 }
-__device__ __forceinline__ void forward_colour(const Smem& s, uint32_t wrow, uint32_t lane, Chain& c) {
+__device__ __forceinline__ void forward_colour(const __half* w, const __half* xc, uint32_t wrow, uint32_t lane, Chain& c) {
     c.xc[0][0] = pack_h2(c.yd[0][0], c.yd[0][1]);
     c.xc[0][1] = pack_h2(c.yd[0][2], c.yd[0][3]);
     c.xc[0][2] = pack_h2(c.yd[1][0], c.yd[1][1]);
     c.xc[0][3] = pack_h2(c.yd[1][2], c.yd[1][3]);
-    load_a_rowmajor(c.xc[1], s.xc, kS32, wrow, 16, lane);
+    load_a_rowmajor(c.xc[1], xc, kS32, wrow, 16, lane);
     float acc[8][4];
-    gemm_nk<8, 2>(acc, c.xc, s.w + kWC0, kS32, lane);
+    gemm_nk<8, 2>(acc, c.xc, w + kWC0, kS32, lane);
     relu_to_a<8>(acc, c.h1);
-    gemm_nk<8, 4>(acc, c.h1, s.w + kWC1, kS64, lane);
+    gemm_nk<8, 4>(acc, c.h1, w + kWC1, kS64, lane);
     relu_to_a<8>(acc, c.h2);
-    gemm_nk<2, 4>(c.yc, c.h2, s.w + kWC2, kS64, lane);
+    gemm_nk<2, 4>(c.yc, c.h2, w + kWC2, kS64, lane);
 }
 
 __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, const int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const Smem s = carve(smem_raw, false);
+    const Smem s = carve(smem_raw);
     const uint32_t n = row_count(a, mode);
     if (n == 0u) return;
     const __half* mlp = static_cast<const __half*>(a.params16) + a.mlp_offset;
     load_weights(s.w, mlp, mode == kFieldOccupancy);
-    load_levels(a, s);
+    load_levels(a.lt, s.lv);
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t n_tiles = (n + kRows - 1u) / kRows;
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    const bool staged = mode == kFieldTrain;
+    if (staged && blockIdx.x < n_tiles) fwd_prefetch(a, fwd_stage(smem_raw, 0), blockIdx.x * kRows, n);
+    cp_async_commit();
+    uint32_t it = 0;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row0 = tile * kRows;
-        __syncthreads();  // previous tile done with shared memory; weights/levels visible
-        load_rows(a, mode, s, row0, n);
+        const FwdStage cur = fwd_stage(smem_raw, it & 1u);
+        if (staged && tile + gridDim.x < n_tiles) fwd_prefetch(a, fwd_stage(smem_raw, (it + 1u) & 1u), (tile + gridDim.x) * kRows, n);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();  // this tile's stage is visible; the previous tile is done with shared memory
+        load_rows(a, mode, s, &cur, row0, n);
         __syncthreads();
         encode_tile(a, s, row0, n, mode != kFieldOccupancy && a.feat != nullptr);
         __syncthreads();
         const uint32_t wrow = warp * 16u;
         Chain c;
-        forward_density(s, wrow, lane, c);
+        forward_density(s.w, s.feat, wrow, lane, c);
         const uint32_t rA = row0 + wrow + g, rB = rA + 8u;
         if (mode == kFieldOccupancy) {
             if (t == 0u) {
@@ -349,7 +418,7 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
             }
             continue;
         }
-        forward_colour(s, wrow, lane, c);
+        forward_colour(s.w, s.xc, wrow, lane, c);
         const float bA = __shfl_down_sync(0xffffffffu, c.yc[0][0], 1);
         const float bB = __shfl_down_sync(0xffffffffu, c.yc[0][2], 1);
         if (t == 0u) {
@@ -357,6 +426,7 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
             if (rB < n) a.raw[rB] = make_float4(c.yd[0][2], c.yc[0][2], c.yc[0][3], bB);
         }
     }
+    cp_async_wait<0>();
 }
 
 // ---- weight-gradient ownership: warp w accumulates 20 m16n8 tiles ----
@@ -391,13 +461,84 @@ __device__ __forceinline__ void store_wtiles(const float (*acc)[4], float* out, 
     }
 }
 
+// Backward: copies of the next tile's features, upstream gradients and row
+// inputs (training: pos+dt and ray id; direct: unit position and direction).
+__device__ __forceinline__ void bwd_prefetch(const FieldArgs& a, int mode, const BwdStage& st, uint32_t row0, uint32_t n) {
+    const uint32_t tid = threadIdx.x;
+    const __half* gf = static_cast<const __half*>(a.feat);
+    for (uint32_t c = tid; c < kRows * 4u; c += kThreads) {
+        const uint32_t r = c >> 2, q = c & 3u;
+        const bool ok = row0 + r < n;
+        cp_async16(st.feat + r * kS32 + q * 8u, gf + (ok ? (static_cast<unsigned long long>(row0 + r) * 32u + q * 8u) : 0ull), ok);
+    }
+    if (tid < kRows) {
+        const uint32_t r = row0 + tid;
+        const bool ok = r < n;
+        cp_async16(st.dout + tid, a.dout + (ok ? r : 0u), ok);
+        if (mode == kFieldTrain) {
+            cp_async16(st.pos + tid, a.pos_dt + (ok ? r : 0u), ok);
+        } else {
+            float* pp = reinterpret_cast<float*>(st.pos + tid);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) cp_async4(pp + k, a.pos_unit + (ok ? 3ull * r + k : 0ull), ok);
+        }
+    } else {
+        const uint32_t i = tid - kRows;
+        const uint32_t r = row0 + i;
+        const bool ok = r < n;
+        if (mode == kFieldTrain) {
+            cp_async4(st.sray + i, a.sample_ray + (ok ? r : 0u), ok);
+        } else {
+            float* dd = reinterpret_cast<float*>(st.dir + i);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) cp_async4(dd + k, a.dirs + (ok ? 3ull * r + k : 0ull), ok);
+        }
+    }
+}
+
+// Coarse levels 0..3 (one per lane position t): a warp's 16 rows are usually
+// consecutive samples of one ray and fall in the same cell.  When the 8 lanes
+// of a level agree on the cell for both of their rows, the 16 contributions
+// per corner are summed in registers and one lane issues the reduction.
+__device__ __forceinline__ void scatter_coarse(uint32_t* G, const LevelParams lp, uint32_t hash_mask, const float pA[3],
+                                               bool okA, float a0, float a1, const float pB[3], bool okB, float b0,
+                                               float b1, uint32_t lane) {
+    uint32_t iA[8], iB[8];
+    float wA[8], wB[8];
+    level_corners(pA, lp, hash_mask, iA, wA);
+    level_corners(pB, lp, hash_mask, iB, wB);
+    const uint32_t t = lane & 3u, gm = 0x11111111u << t;
+    const uint32_t key = okA ? iA[0] : (0xFFFFFFFFu - lane);  // invalid rows never match
+    const uint32_t m = __match_any_sync(0xffffffffu, key);
+    const bool same = ((m & gm) == gm) && okA && okB && iA[0] == iB[0];
+    const uint32_t bal = __ballot_sync(0xffffffffu, same);
+    if ((bal & gm) == gm) {
+#pragma unroll
+        for (int c = 0; c < 8; c += 2) {
+            float s[4] = {__fmaf_rn(wA[c], a0, wB[c] * b0), __fmaf_rn(wA[c], a1, wB[c] * b1),
+                          __fmaf_rn(wA[c + 1], a0, wB[c + 1] * b0), __fmaf_rn(wA[c + 1], a1, wB[c + 1] * b1)};
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) s[k] += __shfl_xor_sync(gm, s[k], o);
+            if (lane == t) red_pair(G, iA[c], iA[c + 1], pack_h2(s[0], s[1]), pack_h2(s[2], s[3]));
+        }
+    } else {
+#pragma unroll
+        for (int c = 0; c < 8; c += 2) {
+            if (okA) red_pair(G, iA[c], iA[c + 1], pack_h2(wA[c] * a0, wA[c] * a1), pack_h2(wA[c + 1] * a0, wA[c + 1] * a1));
+            if (okB) red_pair(G, iB[c], iB[c + 1], pack_h2(wB[c] * b0, wB[c] * b1), pack_h2(wB[c + 1] * b0, wB[c + 1] * b1));
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs a, const int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const Smem s = carve(smem_raw, true);
+    const BwdSmem s = carve_bwd(smem_raw);
     const uint32_t n = row_count(a, mode);
     const __half* mlp = static_cast<const __half*>(a.params16) + a.mlp_offset;
     load_weights(s.w, mlp, false);
-    load_levels(a, s);
+    load_levels(a.lt, s.lv);
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t g = lane >> 2, t = lane & 3u;
     uint32_t* ggrad = static_cast<uint32_t*>(a.grid_grad);
@@ -406,16 +547,46 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
     for (int i = 0; i < 20; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.0f;
 
     const uint32_t n_tiles = (n + kRows - 1u) / kRows;
-    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
+    if (blockIdx.x < n_tiles) bwd_prefetch(a, mode, bwd_stage(smem_raw, 0), blockIdx.x * kRows, n);
+    cp_async_commit();
+    uint32_t it = 0;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t row0 = tile * kRows;
-        __syncthreads();
-        load_rows(a, mode, s, row0, n);
-        load_feat_tile(a, s, row0, n);
-        __syncthreads();
+        const BwdStage cur = bwd_stage(smem_raw, it & 1u);
+        if (tile + gridDim.x < n_tiles) bwd_prefetch(a, mode, bwd_stage(smem_raw, (it + 1u) & 1u), (tile + gridDim.x) * kRows, n);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();  // this tile's stage is visible; the previous tile's weight gradients are done
         const uint32_t wrow = warp * 16u;
+        // Each warp prepares its own 16 rows: unit position (in place) and SH.
+        if (lane < 16u) {
+            const uint32_t rr = wrow + lane;
+            const bool ok = row0 + rr < n;
+            float d[3] = {0.0f, 0.0f, 0.0f};
+            if (mode == kFieldTrain) {
+                const float4 p = cur.pos[rr];
+                const float pw[3] = {p.x, p.y, p.z};
+                float u[3];
+                world_to_unit(a, pw, u);
+                cur.pos[rr] = make_float4(u[0], u[1], u[2], 0.0f);
+                if (ok) {
+                    const RayRecord& ray = a.rays[cur.sray[rr]];
+                    d[0] = ray.dir[0];
+                    d[1] = ray.dir[1];
+                    d[2] = ray.dir[2];
+                }
+            } else {
+                const float4 q = cur.dir[rr];
+                d[0] = q.x;
+                d[1] = q.y;
+                d[2] = q.z;
+            }
+            write_sh(s.xc + rr * kS32, d, ok);
+        }
+        __syncwarp();
         Chain c;
-        forward_density(s, wrow, lane, c);
-        forward_colour(s, wrow, lane, c);
+        forward_density(s.w, cur.feat, wrow, lane, c);
+        forward_colour(s.w, s.xc, wrow, lane, c);
 #pragma unroll
         for (uint32_t kc = 0; kc < 4; ++kc) {
             store_a(s.hd, kS64, wrow, kc, c.hd[kc], lane);
@@ -425,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         store_a(s.xc, kS32, wrow, 0, c.xc[0], lane);
 
         const uint32_t rA = row0 + wrow + g, rB = rA + 8u;
-        const float4 dA = rA < n ? a.dout[rA] : make_float4(0.f, 0.f, 0.f, 0.f);
-        const float4 dB = rB < n ? a.dout[rB] : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 dA = cur.dout[wrow + g];  // zero-filled past the last row
+        const float4 dB = cur.dout[wrow + g + 8u];
         uint32_t dyc[1][4];
         dyc[0][0] = t == 0u ? pack_h2(dA.y, dA.z) : (t == 1u ? pack_h2(dA.w, 0.0f) : 0u);
         dyc[0][1] = t == 0u ? pack_h2(dB.y, dB.z) : (t == 1u ? pack_h2(dB.w, 0.0f) : 0u);
@@ -462,10 +633,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
 
         // Hash-table scatter straight from the dX fragments: this lane holds
         // levels t, t+4, t+8, t+12 of rows g and g+8.
-        const float4 pA4 = s.pos[wrow + g], pB4 = s.pos[wrow + g + 8u];
+        const float4 pA4 = cur.pos[wrow + g], pB4 = cur.pos[wrow + g + 8u];
         const float pA[3] = {pA4.x, pA4.y, pA4.z}, pB[3] = {pB4.x, pB4.y, pB4.z};
+        scatter_coarse(ggrad, s.lv[t], a.lt.hash_mask, pA, rA < n, dxd[0][0], dxd[0][1], pB, rB < n, dxd[0][2], dxd[0][3], lane);
 #pragma unroll
-        for (uint32_t nt = 0; nt < 4; ++nt) {
+        for (uint32_t nt = 1; nt < 4; ++nt) {
             const LevelParams lp = s.lv[4u * nt + t];
             if (rA < n) level_backward(ggrad, pA, lp, a.lt.hash_mask, dxd[nt][0], dxd[nt][1]);
             if (rB < n) level_backward(ggrad, pB, lp, a.lt.hash_mask, dxd[nt][2], dxd[nt][3]);
@@ -475,7 +647,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         // Weight gradients of the tile, summed into this warp's owned tiles.
         if (warp == 0u) {
 #pragma unroll
-            for (uint32_t mt = 0; mt < 4; ++mt) wgrad_rows<4>(acc + 4 * mt, s.dhd, kS64, 16u * mt, s.feat, kS32, 0u, lane);
+            for (uint32_t mt = 0; mt < 4; ++mt) wgrad_rows<4>(acc + 4 * mt, s.dhd, kS64, 16u * mt, cur.feat, kS32, 0u, lane);
             wgrad_rows<4>(acc + 16, s.dyd, kS16, 0u, s.hd, kS64, 0u, lane);
         } else if (warp == 1u) {
             wgrad_rows<4>(acc, s.dyd, kS16, 0u, s.hd, kS64, 32u, lane);
@@ -490,7 +662,9 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
             for (uint32_t mt = 0; mt < 2; ++mt) wgrad_rows<8>(acc + 8 * mt, s.dh2, kS64, 32u + 16u * mt, s.h1, kS64, 0u, lane);
             wgrad_rows<4>(acc + 16, s.dyc, kS16, 0u, s.h2, kS64, 32u, lane);
         }
+        __syncthreads();
     }
+    cp_async_wait<0>();
 
     float* out = a.partials + static_cast<unsigned long long>(blockIdx.x) * kMlpParams;
     if (warp == 0u) {
@@ -512,7 +686,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
     }
 }
 
-
 // ---------------------------------------------------------------------------
 // Renderer.  Persistent CTAs of 4 warps own 64 ray slots.  Every round each
 // live slot marches its ray to the next occupied sample (cone-angle steps,
@@ -529,7 +702,7 @@ struct alignas(16) RenderSlot {
     float T, acc0, acc1, acc2;
     uint32_t i, pixel, n, live;  // live: 0 empty, 1 marching, 2 no work left
 };
-constexpr size_t kRenderSmem = kFwdSmem + kRows * sizeof(RenderSlot) + kRows * 16 + kRows * 4;
+constexpr size_t kRenderSmem = kFwdBase + kRows * sizeof(RenderSlot) + kRows * 16 + kRows * 4;
 
 __device__ __forceinline__ uint32_t pack_rgba(float r, float g, float b) {
     const uint32_t ur = __float2uint_rn(fminf(1.0f, fmaxf(0.0f, r)) * 255.0f);
@@ -540,8 +713,8 @@ __device__ __forceinline__ uint32_t pack_rgba(float r, float g, float b) {
 
 __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const Smem s = carve(smem_raw, false);
-    RenderSlot* slots = reinterpret_cast<RenderSlot*>(smem_raw + kFwdSmem);
+    const Smem s = carve(smem_raw);
+    RenderSlot* slots = reinterpret_cast<RenderSlot*>(smem_raw + kFwdBase);
     float4* raw_s = reinterpret_cast<float4*>(slots + kRows);
     float* dt_s = reinterpret_cast<float*>(raw_s + kRows);
     const __half* mlp = static_cast<const __half*>(a.params16) + a.mlp_offset;
@@ -691,8 +864,8 @@ __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
         {
             const uint32_t wrow = warp * 16u;
             Chain c;
-            forward_density(s, wrow, lane, c);
-            forward_colour(s, wrow, lane, c);
+            forward_density(s.w, s.feat, wrow, lane, c);
+            forward_colour(s.w, s.xc, wrow, lane, c);
             const float bA = __shfl_down_sync(0xffffffffu, c.yc[0][0], 1);
             const float bB = __shfl_down_sync(0xffffffffu, c.yc[0][2], 1);
             if (t4 == 0u) {

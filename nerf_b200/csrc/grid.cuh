@@ -51,15 +51,37 @@ NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_
     }
 }
 
-// Interpolated feature pair of one level (packed f16x2).  params: one
-// uint32 (two fp16 features) per entry.
-NB_DEV uint32_t level_forward(const uint32_t* __restrict__ params, const float p[3], const LevelParams lp, uint32_t hash_mask) {
-    uint32_t idx[8];
-    float w[8];
-    level_corners(p, lp, hash_mask, idx, w);
-    uint32_t v[8];
+// Corners c and c|1 differ only in x.  When their entries form an aligned
+// pair (indices differing in bit 0 only: always on hashed levels for even x,
+// on dense levels for an even first index) both are fetched with one 8-byte
+// load and reduced with one 8-byte f16x2 vector reduction.  Level offsets are
+// multiples of 8 entries, so absolute and level-relative parity agree.
+NB_DEV void gather_pair(const uint32_t* __restrict__ P, uint32_t ea, uint32_t eb, uint32_t& va, uint32_t& vb) {
+    if ((ea ^ eb) == 1u) {
+        const uint2 v = __ldg(reinterpret_cast<const uint2*>(P + (ea & ~1u)));
+        va = (ea & 1u) ? v.y : v.x;
+        vb = (ea & 1u) ? v.x : v.y;
+    } else {
+        va = __ldg(P + ea);
+        vb = __ldg(P + eb);
+    }
+}
+NB_DEV void red_pair(uint32_t* G, uint32_t ea, uint32_t eb, uint32_t va, uint32_t vb) {
+    if ((ea ^ eb) == 1u) {
+        const uint32_t lo = (ea & 1u) ? vb : va, hi = (ea & 1u) ? va : vb;
+        asm volatile("red.global.add.noftz.v2.f16x2 [%0], {%1, %2};\n" ::"l"(G + (ea & ~1u)), "r"(lo), "r"(hi) : "memory");
+    } else {
+        red_add_f16x2(G + ea, va);
+        red_add_f16x2(G + eb, vb);
+    }
+}
+
+NB_DEV void gather8(const uint32_t* __restrict__ P, const uint32_t idx[8], uint32_t v[8]) {
 #pragma unroll
-    for (int c = 0; c < 8; ++c) v[c] = __ldg(params + idx[c]);
+    for (int c = 0; c < 8; c += 2) gather_pair(P, idx[c], idx[c + 1], v[c], v[c + 1]);
+}
+
+NB_DEV uint32_t interpolate(const uint32_t v[8], const float w[8]) {
     float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
@@ -70,31 +92,27 @@ NB_DEV uint32_t level_forward(const uint32_t* __restrict__ params, const float p
     return pack_h2(a0, a1);
 }
 
-// Two (point, level) tasks with all 16 gathers issued before any is used.
+// Interpolated feature pair of one level (packed f16x2).  params: one
+// uint32 (two fp16 features) per entry.
+NB_DEV uint32_t level_forward(const uint32_t* __restrict__ params, const float p[3], const LevelParams lp, uint32_t hash_mask) {
+    uint32_t idx[8], v[8];
+    float w[8];
+    level_corners(p, lp, hash_mask, idx, w);
+    gather8(params, idx, v);
+    return interpolate(v, w);
+}
+
+// Two (point, level) tasks with all their gathers issued before any is used.
 NB_DEV void level_forward2(const uint32_t* __restrict__ params, const float pa[3], const LevelParams la, const float pb[3],
                            const LevelParams lb, uint32_t hash_mask, uint32_t& ra, uint32_t& rb) {
-    uint32_t ia[8], ib[8];
+    uint32_t ia[8], ib[8], va[8], vb[8];
     float wa[8], wb[8];
     level_corners(pa, la, hash_mask, ia, wa);
     level_corners(pb, lb, hash_mask, ib, wb);
-    uint32_t va[8], vb[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        va[c] = __ldg(params + ia[c]);
-        vb[c] = __ldg(params + ib[c]);
-    }
-    float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) {
-        const float2 fa = unpack_h2(va[c]);
-        const float2 fb = unpack_h2(vb[c]);
-        a0 = __fmaf_rn(wa[c], fa.x, a0);
-        a1 = __fmaf_rn(wa[c], fa.y, a1);
-        b0 = __fmaf_rn(wb[c], fb.x, b0);
-        b1 = __fmaf_rn(wb[c], fb.y, b1);
-    }
-    ra = pack_h2(a0, a1);
-    rb = pack_h2(b0, b1);
+    gather8(params, ia, va);
+    gather8(params, ib, vb);
+    ra = interpolate(va, wa);
+    rb = interpolate(vb, wb);
 }
 
 // Scatter of one level's feature gradient (d0, d1) to the eight corner
@@ -104,7 +122,8 @@ NB_DEV void level_backward(uint32_t* grad, const float p[3], const LevelParams l
     float w[8];
     level_corners(p, lp, hash_mask, idx, w);
 #pragma unroll
-    for (int c = 0; c < 8; ++c) red_add_f16x2(grad + idx[c], pack_h2(w[c] * d0, w[c] * d1));
+    for (int c = 0; c < 8; c += 2)
+        red_pair(grad, idx[c], idx[c + 1], pack_h2(w[c] * d0, w[c] * d1), pack_h2(w[c + 1] * d0, w[c + 1] * d1));
 }
 
 }  // namespace nb
