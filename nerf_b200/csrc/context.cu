@@ -215,6 +215,7 @@ struct Context {
     // batch
     uint32_t* ray_counts = nullptr;
     uint32_t* masks = nullptr;
+    float* chunk_t = nullptr;
     uint32_t* ray_offset = nullptr;
     uint32_t* ray_slot = nullptr;
     RayRecord* rays = nullptr;
@@ -470,15 +471,17 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     batch.align = model.align;
     batch.size = 0;
     const uint64_t o_rc = batch.add(t.max_rays * 4ull), o_mask = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
+    const uint64_t o_ct = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
     const uint64_t o_bs = batch.add(t.max_rays * 4ull), o_ba = batch.add(t.max_rays * 4ull);
     const uint64_t o_rays = batch.add(t.max_rays * sizeof(RayRecord)), o_ri = batch.add(t.max_rays * 4ull);
-    const uint64_t o_pos = batch.add(cap * 16u), o_sr = batch.add(cap * 4u), o_feat = batch.add(cap * 64u);
+    const uint64_t o_pos = batch.add(cap * 16u), o_sr = batch.add(cap * 4u), o_feat = batch.add(cap * 112u);
     const uint64_t o_raw = batch.add(cap * 16u), o_dout = batch.add(cap * 16u);
     const uint64_t o_part = batch.add(static_cast<uint64_t>(n_partials) * kMlpParams * 4u);
     const uint64_t o_sig = batch.add(std::max<uint32_t>(t.update_count, 1u) * 4ull);
     if (batch.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
     ray_counts = batch.at<uint32_t>(o_rc);
     masks = batch.at<uint32_t>(o_mask);
+    chunk_t = batch.at<float>(o_ct);
     ray_offset = batch.at<uint32_t>(o_bs);
     ray_slot = batch.at<uint32_t>(o_ba);
     rays = batch.at<RayRecord>(o_rays);
@@ -547,6 +550,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     sa.bitfield = bitfield;
     sa.ray_counts = ray_counts;
     sa.masks = masks;
+    sa.chunk_t = chunk_t;
     sa.ray_offset = ray_offset;
     sa.ray_slot = ray_slot;
     sa.rays = rays;

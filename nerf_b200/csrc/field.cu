@@ -29,6 +29,11 @@ namespace {
 constexpr uint32_t kRows = 64;      // rows per tile
 constexpr uint32_t kThreads = 128;  // 4 warps x 16 rows
 constexpr uint32_t kL = 16;         // hash levels feeding the 32-wide MLP input
+// Training rows written by the forward for the backward: 32 hash features
+// (fp16), 16 SH coefficients (fp16) and the unit position (3 fp32 + pad):
+// 112 bytes = 28 words.  The kernel-level entry points use plain 32-feature
+// rows (16 words).
+constexpr uint32_t kTrainRowU32 = 28, kFeatRowU32 = 16;
 
 // Padded shared-memory copies of the five weight matrices (halves).
 constexpr uint32_t kS32 = 40, kS64 = 72, kS16 = 24;
@@ -181,32 +186,35 @@ __device__ __forceinline__ FwdStage fwd_stage(unsigned char* raw, uint32_t k) {
     return st;
 }
 
-// Shared memory of the backward kernel: weights | xc[64][40] | levels |
-// activation staging for the weight gradients (hd, dhd, h1, dh1, h2, dh2
-// [64][72]; dyd, dyc [64][24]) | two input stages (features [64][40], pos+dt,
-// upstream gradient, ray id, direction), filled with cp.async one tile ahead.
+// Shared memory of the backward kernel: weights | levels | activation
+// staging for the weight gradients (hd, dhd, h1, dh1, h2, dh2 [64][72];
+// dyd, dyc [64][24]) | two input stages (features [64][40], colour input
+// [64][40] whose columns 16..31 hold the SH coefficients, unit position,
+// upstream gradient), filled with cp.async one tile ahead.
 struct BwdSmem {
     __half* w;
-    __half* xc;
     LevelParams* lv;
     __half *hd, *dhd, *h1, *dh1, *h2, *dh2, *dyd, *dyc;
+    float2* runs;
 };
 struct BwdStage {
     __half* feat;
+    __half* xc;
     float4* pos;
     float4* dout;
-    float4* dir;
-    uint32_t* sray;
 };
-constexpr size_t kBwdFixed = kWTotal * 2 + kRows * kS32 * 2 + kMaxLevels * 16 + (6 * kRows * kS64 + 2 * kRows * kS16) * 2;
-constexpr size_t kBwdStage = kRows * kS32 * 2 + 3 * kRows * 16 + kRows * 4;
+// Levels 0..kRunLevels-1 are scattered with run merging (scatter_runs); their
+// dX pass through a per-warp [16][kRunLevels + 1] float2 buffer.
+constexpr uint32_t kRunLevels = 8, kRunStride = kRunLevels + 1;
+constexpr size_t kBwdFixed =
+    kWTotal * 2 + kMaxLevels * 16 + (6 * kRows * kS64 + 2 * kRows * kS16) * 2 + (kThreads / 32) * 16 * kRunStride * 8;
+constexpr size_t kBwdStage = 2 * kRows * kS32 * 2 + 2 * kRows * 16;
 constexpr size_t kBwdSmem = kBwdFixed + 2 * kBwdStage;
 
 __device__ __forceinline__ BwdSmem carve_bwd(unsigned char* raw) {
     BwdSmem s{};
     s.w = reinterpret_cast<__half*>(raw);
-    s.xc = s.w + kWTotal;
-    s.lv = reinterpret_cast<LevelParams*>(s.xc + kRows * kS32);
+    s.lv = reinterpret_cast<LevelParams*>(s.w + kWTotal);
     __half* b = reinterpret_cast<__half*>(s.lv + kMaxLevels);
     s.hd = b;
     s.dhd = s.hd + kRows * kS64;
@@ -216,15 +224,15 @@ __device__ __forceinline__ BwdSmem carve_bwd(unsigned char* raw) {
     s.dh2 = s.h2 + kRows * kS64;
     s.dyd = s.dh2 + kRows * kS64;
     s.dyc = s.dyd + kRows * kS16;
+    s.runs = reinterpret_cast<float2*>(s.dyc + kRows * kS16);
     return s;
 }
 __device__ __forceinline__ BwdStage bwd_stage(unsigned char* raw, uint32_t k) {
     BwdStage st;
     st.feat = reinterpret_cast<__half*>(raw + kBwdFixed + k * kBwdStage);
-    st.pos = reinterpret_cast<float4*>(st.feat + kRows * kS32);
+    st.xc = st.feat + kRows * kS32;
+    st.pos = reinterpret_cast<float4*>(st.xc + kRows * kS32);
     st.dout = st.pos + kRows;
-    st.dir = st.dout + kRows;
-    st.sray = reinterpret_cast<uint32_t*>(st.dir + kRows);
     return st;
 }
 
@@ -242,7 +250,7 @@ __device__ __forceinline__ void world_to_unit(const FieldArgs& a, const float pw
     for (int k = 0; k < 3; ++k) u[k] = clamp01(__fdiv_rn(__fsub_rn(pw[k], a.aabb_min[k]), a.aabb_size[k]));
 }
 
-__device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool valid) {
+__device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool valid, uint32_t* row_tail = nullptr) {
     float sh[16];
     if (valid) {
         sh4(d[0], d[1], d[2], sh);
@@ -250,9 +258,16 @@ __device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool 
 #pragma unroll
         for (int k = 0; k < 16; ++k) sh[k] = 0.0f;
     }
-    uint32_t* dst = reinterpret_cast<uint32_t*>(xc_row + 16u);
+    uint32_t w[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) dst[k] = pack_h2(sh[2 * k], sh[2 * k + 1]);
+    for (int k = 0; k < 8; ++k) w[k] = pack_h2(sh[2 * k], sh[2 * k + 1]);
+    uint4* dst = reinterpret_cast<uint4*>(xc_row + 16u);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    if (row_tail) {
+        reinterpret_cast<uint4*>(row_tail)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(row_tail)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
 }
 
 // Training forward: copies of the next tile's pos+dt and ray ids.
@@ -308,12 +323,20 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
         }
     }
     s.pos[tid] = make_float4(u[0], u[1], u[2], 0.0f);
-    write_sh(s.xc + tid * kS32, d, valid && mode != kFieldOccupancy);
+    // Training rows carry SH and unit position for the backward pass.
+    uint32_t* tail = nullptr;
+    if (mode == kFieldTrain && valid && a.feat != nullptr) {
+        uint32_t* row = static_cast<uint32_t*>(a.feat) + static_cast<unsigned long long>(r) * kTrainRowU32;
+        tail = row + 16u;
+        reinterpret_cast<float4*>(row + 24u)[0] = make_float4(u[0], u[1], u[2], 0.0f);
+    }
+    write_sh(s.xc + tid * kS32, d, valid && mode != kFieldOccupancy, tail);
 }
 
 // Hash-grid encode of a tile: 64 rows x 16 levels over 128 threads; each
 // thread keeps one level and walks 8 rows two at a time.
-__device__ __forceinline__ void encode_tile(const FieldArgs& a, const Smem& s, uint32_t row0, uint32_t n, bool store_global) {
+__device__ __forceinline__ void encode_tile(const FieldArgs& a, const Smem& s, uint32_t row0, uint32_t n, bool store_global,
+                                            uint32_t row_u32) {
     const uint32_t tid = threadIdx.x;
     const uint32_t l = tid % kL;
     const LevelParams lp = s.lv[l];
@@ -336,8 +359,8 @@ __device__ __forceinline__ void encode_tile(const FieldArgs& a, const Smem& s, u
         *reinterpret_cast<uint32_t*>(s.feat + ra * kS32 + 2u * l) = va;
         *reinterpret_cast<uint32_t*>(s.feat + rb * kS32 + 2u * l) = vb;
         if (store_global) {
-            if (oka) gfeat[static_cast<unsigned long long>(row0 + ra) * kL + l] = va;
-            if (okb) gfeat[static_cast<unsigned long long>(row0 + rb) * kL + l] = vb;
+            if (oka) gfeat[static_cast<unsigned long long>(row0 + ra) * row_u32 + l] = va;
+            if (okb) gfeat[static_cast<unsigned long long>(row0 + rb) * row_u32 + l] = vb;
         }
     }
 }
@@ -405,7 +428,8 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
         __syncthreads();  // this tile's stage is visible; the previous tile is done with shared memory
         load_rows(a, mode, s, &cur, row0, n);
         __syncthreads();
-        encode_tile(a, s, row0, n, mode != kFieldOccupancy && a.feat != nullptr);
+        encode_tile(a, s, row0, n, mode != kFieldOccupancy && a.feat != nullptr,
+                    mode == kFieldTrain ? kTrainRowU32 : kFeatRowU32);
         __syncthreads();
         const uint32_t wrow = warp * 16u;
         Chain c;
@@ -461,74 +485,80 @@ __device__ __forceinline__ void store_wtiles(const float (*acc)[4], float* out, 
     }
 }
 
-// Backward: copies of the next tile's features, upstream gradients and row
-// inputs (training: pos+dt and ray id; direct: unit position and direction).
+// Backward: copies of the next tile's inputs.  Training: the 112-byte rows of
+// the forward (features -> feat, SH -> xc[:,16:32], unit position -> pos) and
+// the upstream gradient.  Direct (kernel-level entry): 64-byte feature rows,
+// unit positions and the upstream gradient (SH is computed in the tile).
 __device__ __forceinline__ void bwd_prefetch(const FieldArgs& a, int mode, const BwdStage& st, uint32_t row0, uint32_t n) {
     const uint32_t tid = threadIdx.x;
-    const __half* gf = static_cast<const __half*>(a.feat);
-    for (uint32_t c = tid; c < kRows * 4u; c += kThreads) {
-        const uint32_t r = c >> 2, q = c & 3u;
-        const bool ok = row0 + r < n;
-        cp_async16(st.feat + r * kS32 + q * 8u, gf + (ok ? (static_cast<unsigned long long>(row0 + r) * 32u + q * 8u) : 0ull), ok);
+    const uint4* gr = static_cast<const uint4*>(a.feat);
+    if (mode == kFieldTrain) {
+        for (uint32_t c = tid; c < kRows * 7u; c += kThreads) {
+            const uint32_t r = c / 7u, q = c % 7u;
+            const bool ok = row0 + r < n;
+            void* dst = q < 4u ? static_cast<void*>(st.feat + r * kS32 + q * 8u)
+                               : (q < 6u ? static_cast<void*>(st.xc + r * kS32 + 16u + (q - 4u) * 8u) : static_cast<void*>(st.pos + r));
+            cp_async16(dst, gr + (ok ? static_cast<unsigned long long>(row0 + r) * 7u + q : 0ull), ok);
+        }
+    } else {
+        for (uint32_t c = tid; c < kRows * 4u; c += kThreads) {
+            const uint32_t r = c >> 2, q = c & 3u;
+            const bool ok = row0 + r < n;
+            cp_async16(st.feat + r * kS32 + q * 8u, gr + (ok ? static_cast<unsigned long long>(row0 + r) * 4u + q : 0ull), ok);
+        }
+        if (tid >= kRows) {
+            const uint32_t i = tid - kRows, r = row0 + i;
+            const bool ok = r < n;
+            float* pp = reinterpret_cast<float*>(st.pos + i);
+#pragma unroll
+            for (int k = 0; k < 3; ++k) cp_async4(pp + k, a.pos_unit + (ok ? 3ull * r + k : 0ull), ok);
+        }
     }
     if (tid < kRows) {
         const uint32_t r = row0 + tid;
         const bool ok = r < n;
         cp_async16(st.dout + tid, a.dout + (ok ? r : 0u), ok);
-        if (mode == kFieldTrain) {
-            cp_async16(st.pos + tid, a.pos_dt + (ok ? r : 0u), ok);
-        } else {
-            float* pp = reinterpret_cast<float*>(st.pos + tid);
-#pragma unroll
-            for (int k = 0; k < 3; ++k) cp_async4(pp + k, a.pos_unit + (ok ? 3ull * r + k : 0ull), ok);
-        }
-    } else {
-        const uint32_t i = tid - kRows;
-        const uint32_t r = row0 + i;
-        const bool ok = r < n;
-        if (mode == kFieldTrain) {
-            cp_async4(st.sray + i, a.sample_ray + (ok ? r : 0u), ok);
-        } else {
-            float* dd = reinterpret_cast<float*>(st.dir + i);
-#pragma unroll
-            for (int k = 0; k < 3; ++k) cp_async4(dd + k, a.dirs + (ok ? 3ull * r + k : 0ull), ok);
-        }
     }
 }
 
-// Coarse levels 0..3 (one per lane position t): a warp's 16 rows are usually
-// consecutive samples of one ray and fall in the same cell.  When the 8 lanes
-// of a level agree on the cell for both of their rows, the 16 contributions
-// per corner are summed in registers and one lane issues the reduction.
-__device__ __forceinline__ void scatter_coarse(uint32_t* G, const LevelParams lp, uint32_t hash_mask, const float pA[3],
-                                               bool okA, float a0, float a1, const float pB[3], bool okB, float b0,
-                                               float b1, uint32_t lane) {
-    uint32_t iA[8], iB[8];
-    float wA[8], wB[8];
-    level_corners(pA, lp, hash_mask, iA, wA);
-    level_corners(pB, lp, hash_mask, iB, wB);
-    const uint32_t t = lane & 3u, gm = 0x11111111u << t;
-    const uint32_t key = okA ? iA[0] : (0xFFFFFFFFu - lane);  // invalid rows never match
-    const uint32_t m = __match_any_sync(0xffffffffu, key);
-    const bool same = ((m & gm) == gm) && okA && okB && iA[0] == iB[0];
-    const uint32_t bal = __ballot_sync(0xffffffffu, same);
-    if ((bal & gm) == gm) {
+// Scatter of one coarse level for the 16 rows of a half warp (row r in lane
+// r of the half).  Consecutive rows are consecutive samples, mostly of one
+// ray, and on coarse levels runs of them share a cell.  A segmented suffix sum
+// of the per-corner contributions (w_c * dX rounded to f16x2, summed in f16x2
+// like the L2 reductions they replace) leaves each run's total in its first
+// row, which alone issues the corner reductions: fewer reductions, and far
+// less contention on the hot entries of coarse levels.  Rows of levels whose
+// cell coordinates do not pack into 30 bits (more than 1024 vertices per
+// axis) never merge.
+__device__ __forceinline__ void scatter_runs(uint32_t* G, const LevelParams lp, uint32_t hash_mask, const float p[3], bool ok,
+                                             float d0, float d1, uint32_t r, uint32_t lane) {
+    uint32_t i[3];
+    float f[3], w[8];
+    level_cell(p, lp, i, f);
+    const uint32_t key = (ok && lp.res <= 1024u) ? (i[0] | (i[1] << 10) | (i[2] << 20)) : (0x80000000u | lane);
+    const uint32_t next = __shfl_down_sync(0xffffffffu, key, 1, 16);
+    const uint32_t ends = (__ballot_sync(0xffffffffu, r == 15u || next != key) >> (lane & 16u)) & 0xFFFFu;
+    const uint32_t end = static_cast<uint32_t>(__ffs(ends & (0xFFFFu << r))) - 1u;  // last row of this run
+    const bool head = r == 0u || ((ends >> (r - 1u)) & 1u);
+    corner_weights(f, w);
+    __half2 v[8];
 #pragma unroll
-        for (int c = 0; c < 8; c += 2) {
-            float s[4] = {__fmaf_rn(wA[c], a0, wB[c] * b0), __fmaf_rn(wA[c], a1, wB[c] * b1),
-                          __fmaf_rn(wA[c + 1], a0, wB[c + 1] * b0), __fmaf_rn(wA[c + 1], a1, wB[c + 1] * b1)};
+    for (int c = 0; c < 8; ++c) v[c] = __floats2half2_rn(w[c] * d0, w[c] * d1);
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1)
+    for (uint32_t o = 1; o < 16u; o <<= 1) {
+        const bool take = r + o <= end;
+        if (!__any_sync(0xffffffffu, take)) break;
 #pragma unroll
-                for (int k = 0; k < 4; ++k) s[k] += __shfl_xor_sync(gm, s[k], o);
-            if (lane == t) red_pair(G, iA[c], iA[c + 1], pack_h2(s[0], s[1]), pack_h2(s[2], s[3]));
+        for (int c = 0; c < 8; ++c) {
+            const __half2 x = __shfl_down_sync(0xffffffffu, v[c], o, 16);
+            if (take) v[c] = __hadd2(v[c], x);
         }
-    } else {
+    }
+    if (!(ok && head)) return;
 #pragma unroll
-        for (int c = 0; c < 8; c += 2) {
-            if (okA) red_pair(G, iA[c], iA[c + 1], pack_h2(wA[c] * a0, wA[c] * a1), pack_h2(wA[c + 1] * a0, wA[c + 1] * a1));
-            if (okB) red_pair(G, iB[c], iB[c + 1], pack_h2(wB[c] * b0, wB[c] * b1), pack_h2(wB[c + 1] * b0, wB[c + 1] * b1));
-        }
+    for (uint32_t c = 0; c < 8u; c += 2u) {
+        const uint32_t ea = corner_entry(i, c, lp, hash_mask), eb = corner_entry(i, c + 1u, lp, hash_mask);
+        red_pair(G, ea, eb, *reinterpret_cast<const uint32_t*>(&v[c]), *reinterpret_cast<const uint32_t*>(&v[c + 1]));
     }
 }
 
@@ -558,42 +588,28 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         cp_async_wait<1>();
         __syncthreads();  // this tile's stage is visible; the previous tile's weight gradients are done
         const uint32_t wrow = warp * 16u;
-        // Each warp prepares its own 16 rows: unit position (in place) and SH.
-        if (lane < 16u) {
-            const uint32_t rr = wrow + lane;
-            const bool ok = row0 + rr < n;
-            float d[3] = {0.0f, 0.0f, 0.0f};
-            if (mode == kFieldTrain) {
-                const float4 p = cur.pos[rr];
-                const float pw[3] = {p.x, p.y, p.z};
-                float u[3];
-                world_to_unit(a, pw, u);
-                cur.pos[rr] = make_float4(u[0], u[1], u[2], 0.0f);
-                if (ok) {
-                    const RayRecord& ray = a.rays[cur.sray[rr]];
-                    d[0] = ray.dir[0];
-                    d[1] = ray.dir[1];
-                    d[2] = ray.dir[2];
-                }
-            } else {
-                const float4 q = cur.dir[rr];
-                d[0] = q.x;
-                d[1] = q.y;
-                d[2] = q.z;
+        // Direct rows: each warp computes the SH of its own 16 rows.
+        if (mode != kFieldTrain) {
+            if (lane < 16u) {
+                const uint32_t rr = wrow + lane;
+                const bool ok = row0 + rr < n;
+                float d[3] = {0.0f, 0.0f, 0.0f};
+                if (ok)
+                    for (int k = 0; k < 3; ++k) d[k] = a.dirs[3ull * (row0 + rr) + k];
+                write_sh(cur.xc + rr * kS32, d, ok);
             }
-            write_sh(s.xc + rr * kS32, d, ok);
+            __syncwarp();
         }
-        __syncwarp();
         Chain c;
         forward_density(s.w, cur.feat, wrow, lane, c);
-        forward_colour(s.w, s.xc, wrow, lane, c);
+        forward_colour(s.w, cur.xc, wrow, lane, c);
 #pragma unroll
         for (uint32_t kc = 0; kc < 4; ++kc) {
             store_a(s.hd, kS64, wrow, kc, c.hd[kc], lane);
             store_a(s.h1, kS64, wrow, kc, c.h1[kc], lane);
             store_a(s.h2, kS64, wrow, kc, c.h2[kc], lane);
         }
-        store_a(s.xc, kS32, wrow, 0, c.xc[0], lane);
+        store_a(cur.xc, kS32, wrow, 0, c.xc[0], lane);
 
         const uint32_t rA = row0 + wrow + g, rB = rA + 8u;
         const float4 dA = cur.dout[wrow + g];  // zero-filled past the last row
@@ -631,13 +647,34 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         }
         store_a(s.dyd, kS16, wrow, 0, dyd[0], lane);
 
-        // Hash-table scatter straight from the dX fragments: this lane holds
-        // levels t, t+4, t+8, t+12 of rows g and g+8.
+        // Hash-table scatter.  Coarse levels: dX is transposed through shared
+        // memory to one row per lane of each half warp, half h taking levels
+        // h, h+2, ...; runs of rows in one cell are merged (scatter_runs).
+        float2* runs = s.runs + warp * 16u * kRunStride;
+#pragma unroll
+        for (uint32_t nt = 0; nt < kRunLevels / 4u; ++nt) {
+            runs[g * kRunStride + 4u * nt + t] = make_float2(dxd[nt][0], dxd[nt][1]);
+            runs[(g + 8u) * kRunStride + 4u * nt + t] = make_float2(dxd[nt][2], dxd[nt][3]);
+        }
+        __syncwarp();
+        {
+            const uint32_t r = lane & 15u, h = lane >> 4;
+            const float4 p4 = cur.pos[wrow + r];
+            const float p[3] = {p4.x, p4.y, p4.z};
+            const bool ok = row0 + wrow + r < n;
+#pragma unroll 1
+            for (uint32_t k = 0; k < kRunLevels / 2u; ++k) {
+                const uint32_t l = 2u * k + h;
+                const float2 d = runs[r * kRunStride + l];
+                scatter_runs(ggrad, s.lv[l], a.lt.hash_mask, p, ok, d.x, d.y, r, lane);
+            }
+        }
+        // Fine levels straight from the dX fragments: this lane holds levels
+        // t + 4 nt of rows g and g+8.
         const float4 pA4 = cur.pos[wrow + g], pB4 = cur.pos[wrow + g + 8u];
         const float pA[3] = {pA4.x, pA4.y, pA4.z}, pB[3] = {pB4.x, pB4.y, pB4.z};
-        scatter_coarse(ggrad, s.lv[t], a.lt.hash_mask, pA, rA < n, dxd[0][0], dxd[0][1], pB, rB < n, dxd[0][2], dxd[0][3], lane);
 #pragma unroll
-        for (uint32_t nt = 1; nt < 4; ++nt) {
+        for (uint32_t nt = kRunLevels / 4u; nt < 4; ++nt) {
             const LevelParams lp = s.lv[4u * nt + t];
             if (rA < n) level_backward(ggrad, pA, lp, a.lt.hash_mask, dxd[nt][0], dxd[nt][1]);
             if (rB < n) level_backward(ggrad, pB, lp, a.lt.hash_mask, dxd[nt][2], dxd[nt][3]);
@@ -652,7 +689,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         } else if (warp == 1u) {
             wgrad_rows<4>(acc, s.dyd, kS16, 0u, s.hd, kS64, 32u, lane);
 #pragma unroll
-            for (uint32_t mt = 0; mt < 4; ++mt) wgrad_rows<4>(acc + 4 + 4 * mt, s.dh1, kS64, 16u * mt, s.xc, kS32, 0u, lane);
+            for (uint32_t mt = 0; mt < 4; ++mt) wgrad_rows<4>(acc + 4 + 4 * mt, s.dh1, kS64, 16u * mt, cur.xc, kS32, 0u, lane);
         } else if (warp == 2u) {
 #pragma unroll
             for (uint32_t mt = 0; mt < 2; ++mt) wgrad_rows<8>(acc + 8 * mt, s.dh2, kS64, 16u * mt, s.h1, kS64, 0u, lane);

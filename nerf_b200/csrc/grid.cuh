@@ -25,9 +25,8 @@ struct alignas(16) LevelParams {
 
 NB_DEV float clamp01(float x) { return fminf(1.0f, fmaxf(0.0f, x)); }
 
-NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_mask, uint32_t idx[8], float w[8]) {
-    uint32_t i[3];
-    float f[3];
+// Cell corner i and fractions f of p on one level.
+NB_DEV void level_cell(const float p[3], const LevelParams lp, uint32_t i[3], float f[3]) {
 #pragma unroll
     for (int d = 0; d < 3; ++d) {
         const float u = __fmaf_rn(clamp01(p[d]), lp.scale, 0.5f);
@@ -37,18 +36,32 @@ NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_
         ii = max(0, min(static_cast<int>(lp.res) - 2, ii));
         i[d] = static_cast<uint32_t>(ii);
     }
+}
+// Table entry of corner c of cell i.
+NB_DEV uint32_t corner_entry(const uint32_t i[3], uint32_t c, const LevelParams lp, uint32_t hash_mask) {
+    const uint32_t cx = i[0] + (c & 1u), cy = i[1] + ((c >> 1) & 1u), cz = i[2] + ((c >> 2) & 1u);
+    const uint32_t e = lp.dense ? cx + lp.res * (cy + lp.res * cz) : ((cx ^ (cy * 2654435761u) ^ (cz * 805459861u)) & hash_mask);
+    return lp.offset + e;
+}
+// Trilinear weight of corner c.
+NB_DEV void corner_weights(const float f[3], float w[8]) {
     const float g0[3] = {__fsub_rn(1.0f, f[0]), __fsub_rn(1.0f, f[1]), __fsub_rn(1.0f, f[2])};
 #pragma unroll
     for (uint32_t c = 0; c < 8u; ++c) {
-        const uint32_t cx = i[0] + (c & 1u), cy = i[1] + ((c >> 1) & 1u), cz = i[2] + ((c >> 2) & 1u);
-        const uint32_t e = lp.dense ? cx + lp.res * (cy + lp.res * cz)
-                                    : ((cx ^ (cy * 2654435761u) ^ (cz * 805459861u)) & hash_mask);
-        idx[c] = lp.offset + e;
         const float wx = (c & 1u) ? f[0] : g0[0];
         const float wy = (c & 2u) ? f[1] : g0[1];
         const float wz = (c & 4u) ? f[2] : g0[2];
         w[c] = __fmul_rn(__fmul_rn(wx, wy), wz);
     }
+}
+
+NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_mask, uint32_t idx[8], float w[8]) {
+    uint32_t i[3];
+    float f[3];
+    level_cell(p, lp, i, f);
+#pragma unroll
+    for (uint32_t c = 0; c < 8u; ++c) idx[c] = corner_entry(i, c, lp, hash_mask);
+    corner_weights(f, w);
 }
 
 // Corners c and c|1 differ only in x.  When their entries form an aligned

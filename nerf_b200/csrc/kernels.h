@@ -45,7 +45,7 @@ struct FieldArgs {
     const float* pos_unit;
     const float* dirs;
     // outputs / inputs
-    void* feat;            // fp16 n x 32 (forward writes, backward reads)
+    void* feat;            // training: 112-byte rows (features, SH, unit position); direct: fp16 n x 32
     float4* raw;           // forward: raw sigma, raw rgb
     const float4* dout;    // backward: loss-scaled d raw
     void* grid_grad;       // backward: fp16 entries x 2 (reduction target)
@@ -66,6 +66,7 @@ struct SamplerArgs {
     const uint32_t* bitfield;
     uint32_t* ray_counts;     // [max_rays]
     uint32_t* masks;          // [mask_words][max_rays]
+    float* chunk_t;           // [mask_words][max_rays] t at the start of each chunk with samples
     uint32_t* ray_offset;     // [max_rays] exclusive sample prefix
     uint32_t* ray_slot;       // [max_rays] compacted index, or ~0 when not kept
     RayRecord* rays;          // [max_rays] compacted

@@ -74,6 +74,24 @@ NB_DEV bool occupied(const uint32_t* __restrict__ bits, uint32_t R, const AabbCo
     return ((__ldg(bits + (idx >> 5)) >> (idx & 31u)) & 1u) != 0u;
 }
 
+// Bitfield word of the cell holding p (and the bit within it), or ~0u when p
+// lies outside the box: the address half of occupied(), so that the load can
+// be issued well before its bit is tested.
+NB_DEV uint32_t occupancy_word(uint32_t R, const AabbConsts& b, const float p[3], uint32_t& bit) {
+    float rel[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) rel[k] = __fdiv_rn(__fsub_rn(p[k], b.mn[k]), b.size[k]);
+    bit = 0u;
+    if (rel[0] < 0.0f || rel[0] >= 1.0f || rel[1] < 0.0f || rel[1] >= 1.0f || rel[2] < 0.0f || rel[2] >= 1.0f) return 0xFFFFFFFFu;
+    const float Rf = static_cast<float>(R);
+    const uint32_t ix = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[0], Rf)));
+    const uint32_t iy = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[1], Rf)));
+    const uint32_t iz = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[2], Rf)));
+    const uint32_t idx = ix + iy * R + iz * R * R;
+    bit = idx & 31u;
+    return idx >> 5;
+}
+
 // One step of the cone-angle march (reference backend-cuda.cu:455-468):
 // dt = min(max(dt_min, t*cone), t_far - t), midpoint t + dt/2.
 NB_DEV float march_dt(float t, float tf, float dt_min, float cone) {

@@ -91,19 +91,42 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_count(const SamplerArg
             const float dt_min = __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps));
             float t = ray.tn;
             uint32_t i = 0u;
+            // Software pipeline: the bitfield words of chunk c are loaded while
+            // the step recurrence of chunk c+1 runs.
+            float t_cur = t, mid = 0.0f, dt = 0.0f;
+            uint32_t nv_cur = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
+            uint32_t bit_cur = 0u, w = 0xFFFFFFFFu;
+            if (lane < nv_cur) {
+                float p[3];
+                ray_point(ray, mid, p);
+                w = occupancy_word(tc.grid_res, box, p, bit_cur);
+            }
+            uint32_t word_cur = w != 0xFFFFFFFFu ? __ldg(a.bitfield + w) : 0u;
             for (uint32_t c = 0;; ++c) {
-                float mid = 0.0f, dt = 0.0f;
-                const uint32_t nv = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
-                bool occ = false;
-                if (lane < nv) {
-                    float p[3];
-                    ray_point(ray, mid, p);
-                    occ = occupied(a.bitfield, tc.grid_res, box, p);
+                const float t_next = t;
+                uint32_t nv_next = 0u, bit_next = 0u, word_next = 0u;
+                if (nv_cur == 32u) {
+                    nv_next = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
+                    uint32_t wn = 0xFFFFFFFFu;
+                    if (lane < nv_next) {
+                        float p[3];
+                        ray_point(ray, mid, p);
+                        wn = occupancy_word(tc.grid_res, box, p, bit_next);
+                    }
+                    word_next = wn != 0xFFFFFFFFu ? __ldg(a.bitfield + wn) : 0u;
                 }
+                const bool occ = lane < nv_cur && ((word_cur >> bit_cur) & 1u);
                 const uint32_t bits = __ballot_sync(0xffffffffu, occ);
-                if (nv > 0u && lane == 0u) a.masks[c * tc.max_rays + r] = bits;
+                if (nv_cur > 0u && lane == 0u) {
+                    a.masks[c * tc.max_rays + r] = bits;
+                    if (bits) a.chunk_t[c * tc.max_rays + r] = t_cur;  // pass 2 resumes the march here
+                }
                 count += __popc(bits);
-                if (nv < 32u) break;
+                if (nv_cur < 32u || nv_next == 0u) break;
+                nv_cur = nv_next;
+                bit_cur = bit_next;
+                word_cur = word_next;
+                t_cur = t_next;
             }
         }
     }
@@ -182,9 +205,10 @@ __global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs 
     }
 }
 
-// Pass 2: one warp per kept ray.  The same step recurrence is re-walked; the
-// pass-1 bit words say which steps are samples, and lane j writes step
-// 32c+j at its rank among the chunk's set bits.
+// Pass 2: one warp per kept ray.  Chunks without samples are skipped; a
+// chunk with samples re-walks its 32 steps of the recurrence from the t that
+// pass 1 recorded at its start, and lane j writes step 32c+j at its rank
+// among the chunk's set bits.
 __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     __shared__ float cam[16];
@@ -207,14 +231,16 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
     const uint32_t seed = ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r);
     make_ray(tc, box, cam, seed, ray, rpx, rpy);
     const float dt_min = __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps));
-    float t = ray.tn;
-    uint32_t i = 0u, out = excl;
+    uint32_t out = excl;
     const uint32_t end = excl + count;
     for (uint32_t c = 0; out < end; ++c) {
+        const uint32_t bits = a.masks[c * tc.max_rays + r];
+        if (bits == 0u) continue;
+        float t = a.chunk_t[c * tc.max_rays + r];
+        uint32_t i = 32u * c;
         float mid = 0.0f, dt = 0.0f;
         const uint32_t nv = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
         if (nv == 0u) break;
-        const uint32_t bits = a.masks[c * tc.max_rays + r];
         if ((bits >> lane) & 1u) {
             float p[3];
             ray_point(ray, mid, p);
@@ -223,7 +249,6 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
             a.sample_ray[o] = slot;
         }
         out += __popc(bits);
-        if (nv < 32u) break;
     }
     if (lane != 0u) return;
     a.ray_index[slot] = r;
