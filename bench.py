@@ -52,6 +52,12 @@ WORKLOAD = ("config2 bounded training: 12 spheres/boxes, 100 views 800x800, hash
             "2^18 target samples/step/GPU, <=1024 steps/ray, 128^3 occupancy every 16 steps, random bg")
 
 
+# Kernel launches of one training step: occupancy query and update, the
+# sampler's bitfield / scan / write kernels, field forward, composite, field
+# backward, weight-gradient reduce, statistics, Adam and the next step's march.
+KERNELS_PER_STEP = 12
+
+
 def options(nb, **kw):
     return nb.default_options(log2_hashmap_size=19, max_resolution=2048, background=1, stop_transmittance=1e-4,
                               target_samples_per_step=TARGET_SAMPLES, max_samples_per_step=2 * TARGET_SAMPLES, **kw)
@@ -243,7 +249,7 @@ def run_ours(args):
                              "reads a 256 MB image set; the 24 MB hash table is meant to stay L2-resident",
                        "final_loss": stats.loss, "dataset_gen_s": gen_s},
             "e2e": e2e,
-            "gpu_launches": 11 * args.steps,
+            "gpu_launches": KERNELS_PER_STEP * args.steps,
             "roofline": roofline(dom, hbm, src),
             "kernels": kernels,
             "render": render,

@@ -66,9 +66,10 @@ NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out
 NERF_API NerfStatus nerf_b200_context_stream(void* context, void** stream);
 /* One training step launched kernel by kernel instead of as the captured
  * graph, with CUDA events between launches.  Segments: occupancy query,
- * occupancy update, sampler (count + write), field forward, composite,
- * field backward, weight-gradient reduce, gradient all-reduce (0 on one
- * GPU), gradient statistics, Adam. */
+ * occupancy update, sampler (bitfield tests, compaction scan, sample
+ * writes), field forward, composite, field backward, weight-gradient
+ * reduce, gradient all-reduce (0 on one GPU), gradient statistics, Adam
+ * (with the next step's ray march running beside it on a second stream). */
 #define NERF_B200_STEP_KERNELS 10
 typedef struct NerfB200StepProfile {
     float milliseconds[NERF_B200_STEP_KERNELS];

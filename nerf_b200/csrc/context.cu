@@ -187,6 +187,8 @@ struct Context {
     std::mutex mu;
     int device = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t side = nullptr;  // the next step's march, beside Adam
+    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     NerfB200Options opt{};
     GridLayout grid{};
     LevelTable lt{};
@@ -215,7 +217,8 @@ struct Context {
     // batch
     uint32_t* ray_counts = nullptr;
     uint32_t* masks = nullptr;
-    float* chunk_t = nullptr;
+    float* steps_t = nullptr;
+    RayGeom* geom = nullptr;
     uint32_t* ray_offset = nullptr;
     uint32_t* ray_slot = nullptr;
     RayRecord* rays = nullptr;
@@ -263,6 +266,11 @@ struct Context {
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
+        if (fork_ev) cudaEventDestroy(fork_ev);
+        if (join_ev) cudaEventDestroy(join_ev);
+        fork_ev = join_ev = nullptr;
+        if (side) cudaStreamDestroy(side);
+        side = nullptr;
         if (comm && g_nccl.loaded) g_nccl.comm_destroy(comm);
         comm = nullptr;
         if (stream) cudaStreamDestroy(stream);
@@ -277,6 +285,7 @@ struct Context {
                            uint32_t max_steps, float stop, uint32_t tile, uint32_t rank, uint32_t world,
                            NerfB200RenderInfo* info);
     FieldArgs field_args() const;
+    SamplerArgs sampler_args() const;
     void fill_aabb(float* mn, float* mx, float* size) const;
 };
 
@@ -333,6 +342,10 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     if (ensure_attributes() != cudaSuccess) return NERF_STATUS_FAILURE;
     if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     if (cudaEventCreate(&ev0) != cudaSuccess || cudaEventCreate(&ev1) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    if (cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    if (cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&join_ev, cudaEventDisableTiming) != cudaSuccess)
+        return NERF_STATUS_CUDA_ERROR;
 
     // model arena
     model.align = std::max<uint64_t>(alignment, 256u);
@@ -470,8 +483,9 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     fwd_blocks = field_forward_blocks();
     batch.align = model.align;
     batch.size = 0;
-    const uint64_t o_rc = batch.add(t.max_rays * 4ull), o_mask = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
-    const uint64_t o_ct = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
+    const uint64_t o_rc = batch.add(2ull * t.max_rays * 4ull), o_mask = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
+    const uint64_t o_st = batch.add(static_cast<uint64_t>(t.max_steps) * t.max_rays * 4u);
+    const uint64_t o_geom = batch.add(t.max_rays * sizeof(RayGeom));
     const uint64_t o_bs = batch.add(t.max_rays * 4ull), o_ba = batch.add(t.max_rays * 4ull);
     const uint64_t o_rays = batch.add(t.max_rays * sizeof(RayRecord)), o_ri = batch.add(t.max_rays * 4ull);
     const uint64_t o_pos = batch.add(cap * 16u), o_sr = batch.add(cap * 4u), o_feat = batch.add(cap * 112u);
@@ -481,7 +495,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     if (batch.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
     ray_counts = batch.at<uint32_t>(o_rc);
     masks = batch.at<uint32_t>(o_mask);
-    chunk_t = batch.at<float>(o_ct);
+    steps_t = batch.at<float>(o_st);
+    geom = batch.at<RayGeom>(o_geom);
     ray_offset = batch.at<uint32_t>(o_bs);
     ray_slot = batch.at<uint32_t>(o_ba);
     rays = batch.at<RayRecord>(o_rays);
@@ -505,6 +520,7 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     NB_TRY(cudaMemsetAsync(v, 0, n_params * 4, stream));
     NB_TRY(cudaMemsetAsync(grid_grad, 0, n_grid * 2, stream));
     NB_TRY(cudaMemsetAsync(mlp_grad, 0, kMlpGradSlots * 4, stream));
+    NB_TRY(launch_march(sampler_args(), stream));  // the first step's march; later ones run inside the steps
     configured = true;
     occupancy_valid = false;
     host_generation = 0;
@@ -515,6 +531,26 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     }
     if (cudaStreamSynchronize(stream) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     return NERF_STATUS_OK;
+}
+
+SamplerArgs Context::sampler_args() const {
+    SamplerArgs sa{};
+    sa.tc = tc;
+    sa.state = state;
+    sa.cams = cams;
+    sa.images = images;
+    sa.bitfield = bitfield;
+    sa.ray_counts = ray_counts;
+    sa.masks = masks;
+    sa.steps_t = steps_t;
+    sa.geom = geom;
+    sa.ray_offset = ray_offset;
+    sa.ray_slot = ray_slot;
+    sa.rays = rays;
+    sa.pos_dt = pos_dt;
+    sa.sample_ray = sample_ray;
+    sa.ray_index = ray_index;
+    return sa;
 }
 
 // The kernels of one training step, in order.  The captured graph and the
@@ -542,21 +578,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     oa.decay = tc.occ_decay;
     oa.threshold = tc.occ_threshold;
 
-    SamplerArgs sa{};
-    sa.tc = tc;
-    sa.state = state;
-    sa.cams = cams;
-    sa.images = images;
-    sa.bitfield = bitfield;
-    sa.ray_counts = ray_counts;
-    sa.masks = masks;
-    sa.chunk_t = chunk_t;
-    sa.ray_offset = ray_offset;
-    sa.ray_slot = ray_slot;
-    sa.rays = rays;
-    sa.pos_dt = pos_dt;
-    sa.sample_ray = sample_ray;
-    sa.ray_index = ray_index;
+    const SamplerArgs sa = sampler_args();
 
     FieldArgs fa = field_args();
     fa.pos_dt = pos_dt;
@@ -613,7 +635,14 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     }
     if ((e = mark()) != cudaSuccess) return e;
     if ((e = launch_grad_stats(op, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if ((e = launch_adam(op, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    // The statistics kernel advanced the frame and set the next ray count:
+    // the next step's march runs on the side stream beside Adam.
+    if ((e = cudaEventRecord(fork_ev, s)) != cudaSuccess || (e = cudaStreamWaitEvent(side, fork_ev, 0)) != cudaSuccess ||
+        (e = launch_march(sa, side)) != cudaSuccess || (e = cudaEventRecord(join_ev, side)) != cudaSuccess)
+        return e;
+    if ((e = launch_adam(op, s)) != cudaSuccess || (e = cudaStreamWaitEvent(s, join_ev, 0)) != cudaSuccess ||
+        (e = mark()) != cudaSuccess)
+        return e;
     return cudaSuccess;
 }
 
@@ -1155,6 +1184,7 @@ NERF_API NerfStatus nerf_b200_set_frame_index(void* context, uint32_t frame) {
     Context* c = as_ctx(context);
     std::lock_guard<std::mutex> lk(c->mu);
     NB_TRY(cudaMemcpyAsync(&c->state->frame_index, &frame, 4, cudaMemcpyHostToDevice, c->stream));
+    if (c->configured) NB_TRY(nb::launch_march(c->sampler_args(), c->stream));  // the march depends on the frame
     NB_TRY(cudaStreamSynchronize(c->stream));
     return NERF_STATUS_OK;
 }
@@ -1168,7 +1198,9 @@ NERF_API NerfStatus nerf_b200_read_batch(void* context, uint32_t* ray_counts, ui
     nb::DeviceState st{};
     NB_TRY(cudaMemcpyAsync(&st, c->state, sizeof(st), cudaMemcpyDeviceToHost, c->stream));
     NB_TRY(cudaStreamSynchronize(c->stream));
-    if (ray_counts) NB_TRY(cudaMemcpy(ray_counts, c->ray_counts, st.last_rays * 4ull, cudaMemcpyDeviceToHost));
+    if (ray_counts)
+        NB_TRY(cudaMemcpy(ray_counts, c->ray_counts + static_cast<uint64_t>(st.counts_parity) * c->tc.max_rays,
+                          st.last_rays * 4ull, cudaMemcpyDeviceToHost));
     if (ray_index) NB_TRY(cudaMemcpy(ray_index, c->ray_index, st.last_active * 4ull, cudaMemcpyDeviceToHost));
     if (recs) NB_TRY(cudaMemcpy(recs, c->rays, st.last_active * sizeof(nb::RayRecord), cudaMemcpyDeviceToHost));
     if (pos_dt) NB_TRY(cudaMemcpy(pos_dt, c->pos_dt, st.last_samples * 16ull, cudaMemcpyDeviceToHost));

@@ -195,7 +195,7 @@ struct BwdSmem {
     __half* w;
     LevelParams* lv;
     __half *hd, *dhd, *h1, *dh1, *h2, *dh2, *dyd, *dyc;
-    float2* runs;
+    __half2* runs;
 };
 struct BwdStage {
     __half* feat;
@@ -203,11 +203,11 @@ struct BwdStage {
     float4* pos;
     float4* dout;
 };
-// Levels 0..kRunLevels-1 are scattered with run merging (scatter_runs); their
-// dX pass through a per-warp [16][kRunLevels + 1] float2 buffer.
-constexpr uint32_t kRunLevels = 8, kRunStride = kRunLevels + 1;
+// The hash-table scatter takes dX through a per-warp [16 rows][kL + 1]
+// f16x2 buffer (one row per lane of each half warp, see scatter_runs).
+constexpr uint32_t kRunStride = kL + 1;
 constexpr size_t kBwdFixed =
-    kWTotal * 2 + kMaxLevels * 16 + (6 * kRows * kS64 + 2 * kRows * kS16) * 2 + (kThreads / 32) * 16 * kRunStride * 8;
+    kWTotal * 2 + kMaxLevels * 16 + (6 * kRows * kS64 + 2 * kRows * kS16) * 2 + (kThreads / 32) * 16 * kRunStride * 4;
 constexpr size_t kBwdStage = 2 * kRows * kS32 * 2 + 2 * kRows * 16;
 constexpr size_t kBwdSmem = kBwdFixed + 2 * kBwdStage;
 
@@ -224,7 +224,7 @@ __device__ __forceinline__ BwdSmem carve_bwd(unsigned char* raw) {
     s.dh2 = s.h2 + kRows * kS64;
     s.dyd = s.dh2 + kRows * kS64;
     s.dyc = s.dyd + kRows * kS16;
-    s.runs = reinterpret_cast<float2*>(s.dyc + kRows * kS16);
+    s.runs = reinterpret_cast<__half2*>(s.dyc + kRows * kS16);
     return s;
 }
 __device__ __forceinline__ BwdStage bwd_stage(unsigned char* raw, uint32_t k) {
@@ -521,9 +521,9 @@ __device__ __forceinline__ void bwd_prefetch(const FieldArgs& a, int mode, const
     }
 }
 
-// Scatter of one coarse level for the 16 rows of a half warp (row r in lane
-// r of the half).  Consecutive rows are consecutive samples, mostly of one
-// ray, and on coarse levels runs of them share a cell.  A segmented suffix sum
+// Scatter of one level for the 16 rows of a half warp (row r in lane r of
+// the half).  Consecutive rows are consecutive samples, mostly of one ray,
+// and on all but the finest levels runs of them share a cell.  A segmented suffix sum
 // of the per-corner contributions (w_c * dX rounded to f16x2, summed in f16x2
 // like the L2 reductions they replace) leaves each run's total in its first
 // row, which alone issues the corner reductions: fewer reductions, and far
@@ -611,7 +611,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         }
         store_a(cur.xc, kS32, wrow, 0, c.xc[0], lane);
 
-        const uint32_t rA = row0 + wrow + g, rB = rA + 8u;
         const float4 dA = cur.dout[wrow + g];  // zero-filled past the last row
         const float4 dB = cur.dout[wrow + g + 8u];
         uint32_t dyc[1][4];
@@ -647,14 +646,15 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         }
         store_a(s.dyd, kS16, wrow, 0, dyd[0], lane);
 
-        // Hash-table scatter.  Coarse levels: dX is transposed through shared
-        // memory to one row per lane of each half warp, half h taking levels
-        // h, h+2, ...; runs of rows in one cell are merged (scatter_runs).
-        float2* runs = s.runs + warp * 16u * kRunStride;
+        // Hash-table scatter: dX (rounded to f16x2, the precision of the
+        // table's gradient) is transposed through shared memory to one row
+        // per lane of each half warp, half h taking levels h, h+2, ...; runs
+        // of rows in one cell are merged (scatter_runs).
+        __half2* runs = s.runs + warp * 16u * kRunStride;
 #pragma unroll
-        for (uint32_t nt = 0; nt < kRunLevels / 4u; ++nt) {
-            runs[g * kRunStride + 4u * nt + t] = make_float2(dxd[nt][0], dxd[nt][1]);
-            runs[(g + 8u) * kRunStride + 4u * nt + t] = make_float2(dxd[nt][2], dxd[nt][3]);
+        for (uint32_t nt = 0; nt < 4u; ++nt) {
+            runs[g * kRunStride + 4u * nt + t] = __floats2half2_rn(dxd[nt][0], dxd[nt][1]);
+            runs[(g + 8u) * kRunStride + 4u * nt + t] = __floats2half2_rn(dxd[nt][2], dxd[nt][3]);
         }
         __syncwarp();
         {
@@ -663,21 +663,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
             const float p[3] = {p4.x, p4.y, p4.z};
             const bool ok = row0 + wrow + r < n;
 #pragma unroll 1
-            for (uint32_t k = 0; k < kRunLevels / 2u; ++k) {
+            for (uint32_t k = 0; k < kL / 2u; ++k) {
                 const uint32_t l = 2u * k + h;
-                const float2 d = runs[r * kRunStride + l];
+                const float2 d = __half22float2(runs[r * kRunStride + l]);
                 scatter_runs(ggrad, s.lv[l], a.lt.hash_mask, p, ok, d.x, d.y, r, lane);
             }
-        }
-        // Fine levels straight from the dX fragments: this lane holds levels
-        // t + 4 nt of rows g and g+8.
-        const float4 pA4 = cur.pos[wrow + g], pB4 = cur.pos[wrow + g + 8u];
-        const float pA[3] = {pA4.x, pA4.y, pA4.z}, pB[3] = {pB4.x, pB4.y, pB4.z};
-#pragma unroll
-        for (uint32_t nt = kRunLevels / 4u; nt < 4; ++nt) {
-            const LevelParams lp = s.lv[4u * nt + t];
-            if (rA < n) level_backward(ggrad, pA, lp, a.lt.hash_mask, dxd[nt][0], dxd[nt][1]);
-            if (rB < n) level_backward(ggrad, pB, lp, a.lt.hash_mask, dxd[nt][2], dxd[nt][3]);
         }
         __syncthreads();
 

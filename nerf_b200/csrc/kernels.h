@@ -58,15 +58,24 @@ uint32_t field_backward_blocks();
 cudaError_t field_init_attributes();
 
 // ---- sampler ----
+// Geometry of a marched training ray (48 bytes).
+struct alignas(16) RayGeom {
+    float o[3], d[3];
+    float tf, dt_min;
+    float px, py;       // pixel position of the ray
+    uint32_t n_steps;   // steps of the march (0 when the ray misses the box)
+    uint32_t pad;
+};
 struct SamplerArgs {
     TrainConsts tc;
     DeviceState* state;
     const float* cams;
     const uint8_t* images;
     const uint32_t* bitfield;
-    uint32_t* ray_counts;     // [max_rays]
-    uint32_t* masks;          // [mask_words][max_rays]
-    float* chunk_t;           // [mask_words][max_rays] t at the start of each chunk with samples
+    uint32_t* ray_counts;     // [2][max_rays], half (frame & 1) belongs to the step of that frame
+    uint32_t* masks;          // [max_rays][mask_words] occupancy bits of 32 consecutive steps
+    float* steps_t;           // [max_rays][max_steps] t at the start of each step
+    RayGeom* geom;            // [max_rays]
     uint32_t* ray_offset;     // [max_rays] exclusive sample prefix
     uint32_t* ray_slot;       // [max_rays] compacted index, or ~0 when not kept
     RayRecord* rays;          // [max_rays] compacted
@@ -74,7 +83,12 @@ struct SamplerArgs {
     uint32_t* sample_ray;     // [sample_cap]
     uint32_t* ray_index;      // [max_rays] compacted -> marched ray index
 };
-constexpr uint32_t kSamplerBlock = 256;  // 8 rays (warps) per block
+constexpr uint32_t kSamplerBlock = 256;
+// Step recurrence of every ray of the step whose frame is in the state.  A
+// step's march only depends on the frame and the ray count, so the training
+// step launches the next step's march beside its Adam update.
+cudaError_t launch_march(const SamplerArgs& a, cudaStream_t s);
+// Bitfield tests, compaction scan and sample writes (after launch_march).
 cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s);
 
 // ---- compositing + loss ----

@@ -137,62 +137,82 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     a.mlp_grad[kMlpGradLoss] = 0.0f;
 }
 
-// Adam for 4 consecutive parameters; g holds the loss-scaled gradients.
-// Masters and moments are touched once per step: they are streamed
-// (evict-first) so that they do not push the hash table out of L2.
-__device__ __forceinline__ void adam4(float* master, __half* p16, float* m, float* v, const float g[4], const AdamScalars& s,
-                                      float b1, float b2, float eps) {
-    float4* M4 = reinterpret_cast<float4*>(master);
-    float4* m4 = reinterpret_cast<float4*>(m);
-    float4* v4 = reinterpret_cast<float4*>(v);
-    float4 W = __ldcs(M4), Mm = __ldcs(m4), Vv = __ldcs(v4);
-    float* w = reinterpret_cast<float*>(&W);
-    float* mm = reinterpret_cast<float*>(&Mm);
-    float* vv = reinterpret_cast<float*>(&Vv);
+// Adam state of 4 consecutive parameters: loss-scaled gradients, master
+// weights and moments.  Masters and moments are touched once per step: they
+// are streamed (evict-first) so that they do not push the hash table out of
+// L2.
+struct Chunk {
+    float g[4];
+    float4 w, m, v;
+};
+
+__device__ __forceinline__ void load_chunk(const OptimArgs& a, uint64_t q, uint64_t grid_chunks, Chunk& c) {
+    if (q < grid_chunks) {
+        const uint2 u = static_cast<const uint2*>(a.grid_grad)[q];
+        const float2 f0 = unpack_h2(u.x), f1 = unpack_h2(u.y);
+        c.g[0] = f0.x;
+        c.g[1] = f0.y;
+        c.g[2] = f1.x;
+        c.g[3] = f1.y;
+    } else {
+        const float4 x = reinterpret_cast<const float4*>(a.mlp_grad)[q - grid_chunks];
+        c.g[0] = x.x;
+        c.g[1] = x.y;
+        c.g[2] = x.z;
+        c.g[3] = x.w;
+    }
+    c.w = __ldcs(reinterpret_cast<const float4*>(a.master) + q);
+    c.m = __ldcs(reinterpret_cast<const float4*>(a.m) + q);
+    c.v = __ldcs(reinterpret_cast<const float4*>(a.v) + q);
+}
+
+__device__ __forceinline__ void adam_chunk(const OptimArgs& a, uint64_t q, uint64_t grid_chunks, Chunk& c, const AdamScalars& s) {
+    if (q < grid_chunks) static_cast<uint2*>(a.grid_grad)[q] = make_uint2(0u, 0u);  // cleared for the next step
+    if (s.skip_update) return;
+    float* w = reinterpret_cast<float*>(&c.w);
+    float* mm = reinterpret_cast<float*>(&c.m);
+    float* vv = reinterpret_cast<float*>(&c.v);
+    const float b1 = a.tc.beta1, b2 = a.tc.beta2;
     const float omb1 = __fsub_rn(1.0f, b1), omb2 = __fsub_rn(1.0f, b2);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const float gk = __fmul_rn(__fmul_rn(g[k], s.inv_loss_scale), s.grad_scale);
+        const float gk = __fmul_rn(__fmul_rn(c.g[k], s.inv_loss_scale), s.grad_scale);
         const float mi = __fadd_rn(__fmul_rn(b1, mm[k]), __fmul_rn(omb1, gk));
         const float vi = __fadd_rn(__fmul_rn(b2, vv[k]), __fmul_rn(__fmul_rn(omb2, gk), gk));
         const float num = __fmul_rn(s.learning_rate, __fmul_rn(mi, s.inv_bias_correction1));
-        const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vi, s.inv_bias_correction2)), eps);
+        const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vi, s.inv_bias_correction2)), a.tc.eps);
         w[k] = __fsub_rn(w[k], __fdiv_rn(num, den));
         mm[k] = mi;
         vv[k] = vi;
     }
-    __stcs(M4, W);
-    __stcs(m4, Mm);
-    __stcs(v4, Vv);
-    *reinterpret_cast<uint2*>(p16) = make_uint2(pack_h2(w[0], w[1]), pack_h2(w[2], w[3]));
+    __stcs(reinterpret_cast<float4*>(a.master) + q, c.w);
+    __stcs(reinterpret_cast<float4*>(a.m) + q, c.m);
+    __stcs(reinterpret_cast<float4*>(a.v) + q, c.v);
+    reinterpret_cast<uint2*>(a.params16)[q] = make_uint2(pack_h2(w[0], w[1]), pack_h2(w[2], w[3]));
 }
 
-// One 4-parameter chunk per thread over the flat vector (hash part first).
+// Grid-stride pass over 4-parameter chunks of the flat vector (hash part
+// first).  The loads of the next chunk are issued before the current one is
+// updated, and the first chunk's loads before the step scalars are read, so
+// each thread keeps two chunks of loads in flight.
 __global__ void __launch_bounds__(256) k_adam(const OptimArgs a, const AdamScalars* __restrict__ sp, const AdamScalars direct) {
-    const uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (q >= a.n_params / 4u) return;
+    const uint64_t n_chunks = a.n_params / 4u, grid_chunks = a.n_grid / 4u;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (q >= n_chunks) return;
+    Chunk cur;
+    load_chunk(a, q, grid_chunks, cur);
     const AdamScalars s = sp ? *sp : direct;
-    const uint64_t grid_chunks = a.n_grid / 4u;
-    float g[4];
-    if (q < grid_chunks) {
-        uint2* gg = static_cast<uint2*>(a.grid_grad) + q;
-        const uint2 u = *gg;
-        const float2 f0 = unpack_h2(u.x), f1 = unpack_h2(u.y);
-        g[0] = f0.x;
-        g[1] = f0.y;
-        g[2] = f1.x;
-        g[3] = f1.y;
-        *gg = make_uint2(0u, 0u);  // cleared for the next step's reductions
-    } else {
-        const float4 x = reinterpret_cast<const float4*>(a.mlp_grad)[q - grid_chunks];
-        g[0] = x.x;
-        g[1] = x.y;
-        g[2] = x.z;
-        g[3] = x.w;
+    for (;;) {
+        const uint64_t qn = q + stride;
+        Chunk nxt;
+        const bool more = qn < n_chunks;
+        if (more) load_chunk(a, qn, grid_chunks, nxt);
+        adam_chunk(a, q, grid_chunks, cur, s);
+        if (!more) break;
+        cur = nxt;
+        q = qn;
     }
-    if (s.skip_update) return;
-    adam4(a.master + 4u * q, static_cast<__half*>(a.params16) + 4u * q, a.m + 4u * q, a.v + 4u * q, g, s, a.tc.beta1,
-          a.tc.beta2, a.tc.eps);
 }
 
 __global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, uint64_t n) {
@@ -230,8 +250,9 @@ cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {
 }
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s) {
     const uint64_t chunks = a.n_params / 4u;
-    uint64_t blocks = (chunks + 255u) / 256u;  // one 4-parameter chunk per thread
-    if (blocks > 0x7FFFFFFFull) blocks = 0x7FFFFFFFull;
+    uint64_t blocks = (chunks + 255u) / 256u;
+    const uint64_t cap = 4ull * sm_count();  // 4 resident blocks per SM, grid-stride beyond
+    if (blocks > cap) blocks = cap;
     if (blocks == 0u) blocks = 1u;
     k_adam<<<static_cast<uint32_t>(blocks), 256, 0, s>>>(a, a.state ? &a.state->adam : nullptr, a.direct_scalars);
     return cudaGetLastError();

@@ -4,14 +4,19 @@
 // reference sampler (backend-cuda.cu:422-533): one camera per step, pixel
 // from the hashed RNG, samples at step midpoints kept where the occupancy
 // bitfield is set.  Instead of the reference's two atomic counters (whose
-// order is nondeterministic), compaction is an ordered prefix sum:
-//   pass 1 (k_sample_count): march each ray, record which steps hit occupied
-//     cells in 32-step bit words, count samples; per-block totals.
-//   pass 2 (k_sample_write): each block sums the totals of the blocks before
-//     it, scans its own rays, and re-walks the step recurrence (no occupancy
-//     lookups, only the recorded bits) to write samples at their final
-//     offsets.  Rays are kept in ray order while the running total stays
-//     within the per-step capacity.
+// order is nondeterministic), compaction is an ordered prefix sum, and the
+// one serial part of the march -- the step recurrence t += dt(t) -- is
+// separated from everything that can run in parallel:
+//   k_march        one thread per ray: the ray, its chord and the step
+//                  recurrence, writing t at the start of every step;
+//   k_sample_bits  one warp per (ray, 32-step chunk): lane j tests step
+//                  32c+j against the bitfield; the ballot is the chunk's
+//                  bit word, its popcount is added to the ray's count;
+//   k_sample_scan  ordered exclusive scans of counts and active flags with
+//                  the capacity cut;
+//   k_sample_write one warp per kept ray: samples at their final offsets
+//                  (chunk offsets from a warp scan of the bit-word counts),
+//                  then the ray record with its ground-truth colour.
 // All float arithmetic that decides which steps are kept uses explicit
 // rounding intrinsics, so the CPU oracle reproduces per-ray counts and
 // offsets bit for bit.  (The reference normalises with the approximate
@@ -49,88 +54,125 @@ __device__ __forceinline__ bool make_ray(const TrainConsts& tc, const AabbConsts
     return clip_aabb(b, r);
 }
 
-// The next 32 steps of a ray's march.  Every lane runs the same step
-// recurrence (t is warp-uniform, no divergence) and keeps the step whose
-// index within the chunk equals its lane.  Returns the number of valid steps.
-__device__ __forceinline__ uint32_t march_chunk(const Ray& ray, float dt_min, float cone, uint32_t max_steps, float& t,
-                                                uint32_t& i, uint32_t lane, float& my_mid, float& my_dt) {
-    uint32_t nv = 0u;
-#pragma unroll 4
-    for (uint32_t j = 0; j < 32u; ++j) {
-        if (!(t < ray.tf && i < max_steps)) break;
-        const float dt = march_dt(t, ray.tf, dt_min, cone);
-        if (j == lane) {
-            my_mid = march_mid(t, dt);
-            my_dt = dt;
-        }
-        t = __fadd_rn(t, dt);
-        ++i;
-        ++nv;
-    }
-    return nv;
+// Per-ray sample counts of the step of frame f.
+__device__ __forceinline__ uint32_t* counts_of(const SamplerArgs& a, uint32_t frame) {
+    return a.ray_counts + static_cast<unsigned long long>(frame & 1u) * a.tc.max_rays;
 }
 
-// Pass 1: one warp per ray.  Lane j tests step 32c+j of chunk c; the
-// ballot of the 32 tests is the chunk's bit word.
-__global__ void __launch_bounds__(kSamplerBlock) k_sample_count(const SamplerArgs a) {
+// Step recurrence of one ray per thread (reference backend-cuda.cu:455-468).
+// The chain is serial by definition; t of every step is stored so that the
+// bitfield tests and the sample writes run one lane per step.  Blocks are a
+// single warp, so the few warps of a step spread over the SMs.  Each lane
+// stages 32 steps in shared memory; while the next 32 steps run, the warp
+// writes the staged block out as 128-byte rows of the [ray][step] array, one
+// row per step, filling the latency of the recurrence.
+constexpr uint32_t kMarchBlock = 32;
+
+__device__ __forceinline__ void march_flush_row(const SamplerArgs& a, const float* stage, uint32_t r0, uint32_t k,
+                                                uint32_t base, uint32_t steps_k, uint32_t lane) {
+    if (base + lane < steps_k)
+        a.steps_t[static_cast<unsigned long long>(r0 + k) * a.tc.max_steps + base + lane] = stage[k * 33u + lane];
+}
+
+__global__ void __launch_bounds__(kMarchBlock) k_march(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     __shared__ float cam[16];
+    __shared__ float stage[2][32 * 33];
     const uint32_t frame = a.state->frame_index;
-    const uint32_t n_rays = a.state->n_rays;
-    if (threadIdx.x < 12u) cam[threadIdx.x] = a.cams[16ull * train_camera(frame, tc.n_images) + threadIdx.x];
-    __syncthreads();
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint32_t r = blockIdx.x * (kSamplerBlock / 32u) + (threadIdx.x >> 5);
-    if (r >= tc.max_rays) return;
-    uint32_t count = 0u;
-    if (r < n_rays) {
-        const AabbConsts box = aabb_of(tc);
-        Ray ray;
-        float px, py;
-        if (make_ray(tc, box, cam, ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r), ray, px, py)) {
-            const float dt_min = __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps));
-            float t = ray.tn;
-            uint32_t i = 0u;
-            // Software pipeline: the bitfield words of chunk c are loaded while
-            // the step recurrence of chunk c+1 runs.
-            float t_cur = t, mid = 0.0f, dt = 0.0f;
-            uint32_t nv_cur = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
-            uint32_t bit_cur = 0u, w = 0xFFFFFFFFu;
-            if (lane < nv_cur) {
-                float p[3];
-                ray_point(ray, mid, p);
-                w = occupancy_word(tc.grid_res, box, p, bit_cur);
-            }
-            uint32_t word_cur = w != 0xFFFFFFFFu ? __ldg(a.bitfield + w) : 0u;
-            for (uint32_t c = 0;; ++c) {
-                const float t_next = t;
-                uint32_t nv_next = 0u, bit_next = 0u, word_next = 0u;
-                if (nv_cur == 32u) {
-                    nv_next = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
-                    uint32_t wn = 0xFFFFFFFFu;
-                    if (lane < nv_next) {
-                        float p[3];
-                        ray_point(ray, mid, p);
-                        wn = occupancy_word(tc.grid_res, box, p, bit_next);
-                    }
-                    word_next = wn != 0xFFFFFFFFu ? __ldg(a.bitfield + wn) : 0u;
-                }
-                const bool occ = lane < nv_cur && ((word_cur >> bit_cur) & 1u);
-                const uint32_t bits = __ballot_sync(0xffffffffu, occ);
-                if (nv_cur > 0u && lane == 0u) {
-                    a.masks[c * tc.max_rays + r] = bits;
-                    if (bits) a.chunk_t[c * tc.max_rays + r] = t_cur;  // pass 2 resumes the march here
-                }
-                count += __popc(bits);
-                if (nv_cur < 32u || nv_next == 0u) break;
-                nv_cur = nv_next;
-                bit_cur = bit_next;
-                word_cur = word_next;
-                t_cur = t_next;
-            }
+    const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
+    const uint32_t r0 = blockIdx.x * kMarchBlock;
+    if (r0 >= n_rays) return;  // whole block
+    const uint32_t lane = threadIdx.x;
+    if (lane < 12u) cam[lane] = a.cams[16ull * train_camera(frame, tc.n_images) + lane];
+    __syncwarp();
+    const uint32_t r = r0 + lane;
+    const AabbConsts box = aabb_of(tc);
+    Ray ray{};
+    RayGeom g{};
+    bool live = r < n_rays && make_ray(tc, box, cam, ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r), ray, g.px, g.py);
+    const float dt_min = live ? __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps)) : 0.0f;
+    // Below tf every dt is positive, and once t reaches tf it never drops
+    // below it again (past tf, dt = tf - t is exact and brings t back to tf),
+    // so the steps with t < tf are a prefix: 32 steps run without a per-step
+    // exit test and are counted after.
+    float t = ray.tn;
+    uint32_t i = 0u, i_prev = 0u, blk = 0u;
+    for (uint32_t base = 0; __any_sync(0xffffffffu, live); base += 32u, ++blk) {
+        float* mine = stage[blk & 1u] + lane * 33u;
+        const float* prev = stage[(blk & 1u) ^ 1u];
+        uint32_t nv = 0u;
+#pragma unroll 8
+        for (uint32_t j = 0; j < 32u; ++j) {
+            mine[j] = t;
+            nv += t < ray.tf ? 1u : 0u;
+            t = __fadd_rn(t, march_dt(t, ray.tf, dt_min, tc.cone));
+            const uint32_t steps_j = __shfl_sync(0xffffffffu, i_prev, j);
+            if (base != 0u) march_flush_row(a, prev, r0, j, base - 32u, steps_j, lane);
+        }
+        if (live) {
+            nv = min(nv, tc.max_steps - base);
+            i = base + nv;
+            live = nv == 32u && i < tc.max_steps;
+        }
+        i_prev = i;
+        __syncwarp();
+        if (!__any_sync(0xffffffffu, live)) {  // last block: flush it now
+#pragma unroll 8
+            for (uint32_t k = 0; k < 32u; ++k) march_flush_row(a, mine - lane * 33u, r0, k, base, __shfl_sync(0xffffffffu, i, k), lane);
         }
     }
-    if (lane == 0u) a.ray_counts[r] = count;
+    if (r >= n_rays) return;
+    counts_of(a, frame)[r] = 0u;
+    g.tf = ray.tf;
+    g.dt_min = dt_min;
+    g.n_steps = i;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        g.o[k] = ray.o[k];
+        g.d[k] = ray.d[k];
+    }
+    a.geom[r] = g;
+}
+
+// Midpoint position and dt of step i of a ray.
+__device__ __forceinline__ float step_point(const SamplerArgs& a, const RayGeom& g, uint32_t r, uint32_t i, float p[3]) {
+    const float t = a.steps_t[static_cast<unsigned long long>(r) * a.tc.max_steps + i];
+    const float dt = march_dt(t, g.tf, g.dt_min, a.tc.cone);
+    const float mid = march_mid(t, dt);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) p[k] = __fmaf_rn(mid, g.d[k], g.o[k]);
+    return dt;
+}
+
+__device__ __forceinline__ uint32_t warps_in_grid() { return gridDim.x * (blockDim.x / 32u); }
+__device__ __forceinline__ uint32_t warp_in_grid() { return blockIdx.x * (blockDim.x / 32u) + (threadIdx.x >> 5); }
+
+// Bitfield tests: a grid-stride loop over (ray, chunk) pairs, one warp each.
+__global__ void __launch_bounds__(kSamplerBlock) k_sample_bits(const SamplerArgs a) {
+    const TrainConsts& tc = a.tc;
+    const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
+    uint32_t* counts = counts_of(a, a.state->frame_index);
+    const uint32_t lane = threadIdx.x & 31u;
+    const AabbConsts box = aabb_of(tc);
+    const unsigned long long total = static_cast<unsigned long long>(n_rays) * tc.mask_words;
+    for (unsigned long long w = warp_in_grid(); w < total; w += warps_in_grid()) {
+        const uint32_t r = static_cast<uint32_t>(w / tc.mask_words), c = static_cast<uint32_t>(w % tc.mask_words);
+        const RayGeom& g = a.geom[r];
+        const uint32_t n_steps = g.n_steps;
+        if (32u * c >= n_steps) continue;
+        const uint32_t i = 32u * c + lane;
+        bool occ = false;
+        if (i < n_steps) {
+            float p[3];
+            step_point(a, g, r, i, p);
+            occ = occupied(a.bitfield, tc.grid_res, box, p);
+        }
+        const uint32_t bits = __ballot_sync(0xffffffffu, occ);
+        if (lane == 0u) {
+            a.masks[static_cast<unsigned long long>(r) * tc.mask_words + c] = bits;
+            if (bits) atomicAdd(counts + r, static_cast<uint32_t>(__popc(bits)));
+        }
+    }
 }
 
 // Ordered compaction over all marched rays in one block: exclusive scans of
@@ -141,11 +183,13 @@ constexpr uint32_t kScanThreads = 1024;
 __global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     const uint32_t n = min(a.state->n_rays, tc.max_rays);
+    const uint32_t frame = a.state->frame_index;
+    const uint32_t* counts = counts_of(a, frame);
     const uint32_t per = (n + kScanThreads - 1u) / kScanThreads;
     const uint32_t r0 = threadIdx.x * per, r1 = min(n, r0 + per);
     uint32_t ls = 0u, la = 0u;
     for (uint32_t r = r0; r < r1; ++r) {
-        const uint32_t c = a.ray_counts[r];
+        const uint32_t c = counts[r];
         ls += c;
         la += c > 0u ? 1u : 0u;
     }
@@ -184,7 +228,7 @@ __global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs 
     const uint32_t tot_s = ws[31], tot_a = wa[31];
     const uint32_t cap = tc.sample_cap;
     for (uint32_t r = r0; r < r1; ++r) {
-        const uint32_t c = a.ray_counts[r];
+        const uint32_t c = counts[r];
         const uint32_t incl = ps + c;
         const bool kept = c > 0u && incl <= cap;
         a.ray_offset[r] = ps;
@@ -197,6 +241,7 @@ __global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs 
         pa += c > 0u ? 1u : 0u;
     }
     if (threadIdx.x == 0u) {
+        a.state->counts_parity = frame & 1u;
         a.state->n_marched_active = tot_a;
         if (tot_s <= cap) {
             a.state->n_samples = tot_s;
@@ -205,55 +250,15 @@ __global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs 
     }
 }
 
-// Pass 2: one warp per kept ray.  Chunks without samples are skipped; a
-// chunk with samples re-walks its 32 steps of the recurrence from the t that
-// pass 1 recorded at its start, and lane j writes step 32c+j at its rank
-// among the chunk's set bits.
-__global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
+// Ray record of a kept ray: direction, sample range, background and the
+// ground truth -- a bilinear RGBA8 fetch at the unflipped pixel position,
+// composited on the ray's background (reference backend-cuda.cu:471-499).
+__device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom& g, uint32_t r, uint32_t slot, uint32_t excl,
+                                             uint32_t count, uint32_t frame, uint32_t camera) {
     const TrainConsts& tc = a.tc;
-    __shared__ float cam[16];
-    const uint32_t frame = a.state->frame_index;
-    const uint32_t camera = train_camera(frame, tc.n_images);
-    if (threadIdx.x < 12u) cam[threadIdx.x] = a.cams[16ull * camera + threadIdx.x];
-    __syncthreads();
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint32_t r = blockIdx.x * (kSamplerBlock / 32u) + (threadIdx.x >> 5);
-    if (r >= min(a.state->n_rays, tc.max_rays)) return;
-    const uint32_t count = a.ray_counts[r];
-    if (count == 0u) return;
-    const uint32_t slot = a.ray_slot[r];
-    if (slot == 0xFFFFFFFFu) return;
-    const uint32_t excl = a.ray_offset[r];
-
-    const AabbConsts box = aabb_of(tc);
-    Ray ray;
-    float rpx = 0.0f, rpy = 0.0f;
     const uint32_t seed = ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r);
-    make_ray(tc, box, cam, seed, ray, rpx, rpy);
-    const float dt_min = __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps));
-    uint32_t out = excl;
-    const uint32_t end = excl + count;
-    for (uint32_t c = 0; out < end; ++c) {
-        const uint32_t bits = a.masks[c * tc.max_rays + r];
-        if (bits == 0u) continue;
-        float t = a.chunk_t[c * tc.max_rays + r];
-        uint32_t i = 32u * c;
-        float mid = 0.0f, dt = 0.0f;
-        const uint32_t nv = march_chunk(ray, dt_min, tc.cone, tc.max_steps, t, i, lane, mid, dt);
-        if (nv == 0u) break;
-        if ((bits >> lane) & 1u) {
-            float p[3];
-            ray_point(ray, mid, p);
-            const uint32_t o = out + __popc(bits & ((1u << lane) - 1u));
-            a.pos_dt[o] = make_float4(p[0], p[1], p[2], dt);
-            a.sample_ray[o] = slot;
-        }
-        out += __popc(bits);
-    }
-    if (lane != 0u) return;
+    const float rpx = g.px, rpy = g.py;
     a.ray_index[slot] = r;
-    // Ground truth: bilinear RGBA8 fetch at the unflipped pixel position,
-    // composited on the ray's background (reference backend-cuda.cu:471-499).
     float bg[3] = {1.0f, 1.0f, 1.0f};
     if (tc.background == 1u) {
         bg[0] = rand01(seed ^ kBgSalt0);
@@ -284,9 +289,9 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
         v[ch] = __fmaf_rn(tb, ty, __fmul_rn(ta, omty));
     }
     RayRecord rec;
-    rec.dir[0] = ray.d[0];
-    rec.dir[1] = ray.d[1];
-    rec.dir[2] = ray.d[2];
+    rec.dir[0] = g.d[0];
+    rec.dir[1] = g.d[1];
+    rec.dir[2] = g.d[2];
     rec.begin = excl;
     const float oma = __fsub_rn(1.0f, v[3]);
 #pragma unroll
@@ -299,17 +304,74 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
     a.rays[slot] = rec;
 }
 
+// One warp per kept ray (grid-stride).  Lane k holds the bit word of chunk
+// 32q+k; a warp scan of their counts gives each chunk's offset, and lane j
+// of a chunk with samples writes step 32c+j at its rank among the set bits.
+__global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
+    const TrainConsts& tc = a.tc;
+    const uint32_t frame = a.state->frame_index;
+    const uint32_t camera = train_camera(frame, tc.n_images);
+    const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t* counts = counts_of(a, frame);
+    for (uint32_t r = warp_in_grid(); r < n_rays; r += warps_in_grid()) {
+        const uint32_t count = counts[r];
+        if (count == 0u) continue;
+        const uint32_t slot = a.ray_slot[r];
+        if (slot == 0xFFFFFFFFu) continue;
+        const uint32_t excl = a.ray_offset[r];
+        const RayGeom& g = a.geom[r];
+        const uint32_t* rm = a.masks + static_cast<unsigned long long>(r) * tc.mask_words;
+        const uint32_t n_chunks = (g.n_steps + 31u) / 32u;
+        uint32_t out = excl;
+        for (uint32_t c0 = 0; c0 < n_chunks; c0 += 32u) {
+            const uint32_t mine = c0 + lane < n_chunks ? rm[c0 + lane] : 0u;
+            const uint32_t cnt = __popc(mine);
+            uint32_t incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += x;
+            }
+            const uint32_t base = out + incl - cnt;
+            uint32_t todo = __ballot_sync(0xffffffffu, mine != 0u);
+            while (todo) {
+                const uint32_t k = static_cast<uint32_t>(__ffs(todo)) - 1u;
+                todo &= todo - 1u;
+                const uint32_t bits = __shfl_sync(0xffffffffu, mine, k);
+                const uint32_t at = __shfl_sync(0xffffffffu, base, k);
+                if ((bits >> lane) & 1u) {
+                    float p[3];
+                    const float dt = step_point(a, g, r, 32u * (c0 + k) + lane, p);
+                    const uint32_t o = at + __popc(bits & ((1u << lane) - 1u));
+                    a.pos_dt[o] = make_float4(p[0], p[1], p[2], dt);
+                    a.sample_ray[o] = slot;
+                }
+            }
+            out += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0u) write_record(a, g, r, slot, excl, count, frame, camera);
+    }
+}
+
 }  // namespace
 
+cudaError_t launch_march(const SamplerArgs& a, cudaStream_t s) {
+    k_march<<<(a.tc.max_rays + kMarchBlock - 1u) / kMarchBlock, kMarchBlock, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s) {
-    const uint32_t rays_per_block = kSamplerBlock / 32u;
-    const uint32_t blocks = (a.tc.max_rays + rays_per_block - 1u) / rays_per_block;
-    k_sample_count<<<blocks, kSamplerBlock, 0, s>>>(a);
-    cudaError_t e = cudaGetLastError();
+    int dev = 0, sms = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    const uint32_t warp_blocks = static_cast<uint32_t>(sms) * 8u;  // grid-stride kernels: 8 blocks per SM
+    k_sample_bits<<<warp_blocks, kSamplerBlock, 0, s>>>(a);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     k_sample_scan<<<1, kScanThreads, 0, s>>>(a);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_sample_write<<<blocks, kSamplerBlock, 0, s>>>(a);
+    k_sample_write<<<warp_blocks, kSamplerBlock, 0, s>>>(a);
     return cudaGetLastError();
 }
 

@@ -79,7 +79,7 @@ struct DeviceState {
     uint32_t last_samples;
     uint32_t last_active;
     uint32_t last_rays;
-    uint32_t pad0;
+    uint32_t counts_parity;  // which half of the per-ray count buffer the last step used
     unsigned long long total_samples;
     unsigned long long total_rays;
 };
