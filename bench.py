@@ -354,14 +354,17 @@ def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
     import torch
     import torch.distributed as dist
     steps = args.e2e_steps
-    if world > 1:
+    if world > 1:  # a fresh communicator for this job: NCCL ids are single-use
+        obj = [nb.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        uid = obj[0]
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     ctx = nb.Context(ds_pinned, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
                      options=options(nb))
     if world > 1:
-        ctx.dp_init(rank, world, uid if rank == 0 else uid)
+        ctx.dp_init(rank, world, uid)
     ctx.configure(train_config(nb))
     for _ in range(steps):
         ctx.train_step()

@@ -89,6 +89,17 @@ def training_config(aabb=((-1, -1, -1), (1, 1, 1)), rays=4096, steps=200, lr=1e-
     return NerfTrainingConfig(x0, y0, z0, x1, y1, z1, hp, oc, rays, steps)
 
 
+def create_desc(ds: Dataset, grid_res=128, max_sample_steps=1 << 22, max_batch_rays=1 << 16, alignment=256):
+    """NerfCreateDesc for a dataset, with the host arrays it points to (keep
+    them alive while the descriptor is used)."""
+    images = np.ascontiguousarray(ds.images)
+    cams = np.ascontiguousarray(ds.cameras, dtype=np.float32)
+    fx, fy, cx, cy = ds.intrinsics
+    desc = NerfCreateDesc(grid_res, max_sample_steps, max_batch_rays, alignment, images.ctypes.data, images.nbytes,
+                          cams.ctypes.data, cams.nbytes, ds.n, ds.width, ds.height, fx, fy, cx, cy)
+    return desc, images, cams
+
+
 class Context:
     """One nerf.h context (device = the current CUDA device at creation)."""
 
@@ -96,12 +107,7 @@ class Context:
                  alignment=256):
         self.lib = lib()
         self.ds = ds
-        self._images = np.ascontiguousarray(ds.images)
-        self._cams = np.ascontiguousarray(ds.cameras, dtype=np.float32)
-        fx, fy, cx, cy = ds.intrinsics
-        self.desc = NerfCreateDesc(grid_res, max_sample_steps, max_batch_rays, alignment, self._images.ctypes.data,
-                                   self._images.nbytes, self._cams.ctypes.data, self._cams.nbytes, ds.n, ds.width,
-                                   ds.height, fx, fy, cx, cy)
+        self.desc, self._images, self._cams = create_desc(ds, grid_res, max_sample_steps, max_batch_rays, alignment)
         self.grid_res = grid_res
         self.handle = C.c_void_p()
         opts = options if options is not None else default_options()

@@ -75,6 +75,7 @@ _PROTOS = {
     "oracle_ctx_get_params": (C.c_int, [P, P, P, P, P, P]),
     "oracle_ctx_set_params": (C.c_int, [P, P]),
     "oracle_ctx_set_grads": (C.c_int, [P, P, F32, U32]),
+    "oracle_ctx_get_loss": (C.c_int, [P, P, P]),
     "oracle_ctx_get_occupancy": (C.c_int, [P, P, P]),
     "oracle_ctx_set_occupancy": (C.c_int, [P, P, P]),
     "oracle_ctx_set_frame": (C.c_int, [P, U32]),
@@ -267,6 +268,12 @@ class Context:
     def set_grads(self, grad, loss_sum, active):
         grad = np.ascontiguousarray(grad, np.float32)
         self.lib.oracle_ctx_set_grads(self.h, ptr(grad), loss_sum, active)
+
+    def loss(self):
+        """(normalised loss sum, kept rays) of the pending step."""
+        ls, act = F32(), U32()
+        self.lib.oracle_ctx_get_loss(self.h, C.byref(ls), C.byref(act))
+        return ls.value, act.value
 
     def occupancy(self):
         cells = self.grid_res ** 3

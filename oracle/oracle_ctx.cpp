@@ -599,6 +599,13 @@ int oracle_ctx_set_grads(void* ctx, const float* grad, float loss_sum, uint32_t 
     return NERF_STATUS_OK;
 }
 
+int oracle_ctx_get_loss(void* ctx, float* loss_sum, uint32_t* active_rays) {
+    Ctx* c = static_cast<Ctx*>(ctx);
+    if (loss_sum) *loss_sum = static_cast<float>(c->loss_sum);
+    if (active_rays) *active_rays = c->active;
+    return NERF_STATUS_OK;
+}
+
 int oracle_ctx_get_occupancy(void* ctx, float* density, uint32_t* bitfield) {
     Ctx* c = static_cast<Ctx*>(ctx);
     if (density) std::memcpy(density, c->density.data(), c->density.size() * 4);

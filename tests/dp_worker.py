@@ -1,0 +1,106 @@
+"""Rank bodies of the data-parallel tests (run in spawned processes).
+
+The data-parallel step (reference training step backend-cuda.cu:2216-2401,
+sharded by ray batch): every rank samples its own rays (global ray index
+rank * rays_per_batch + r), normalises its loss by its kept rays times the
+world size, the gradients and the loss are summed over ranks, and every rank
+applies the same Adam update to its replica.
+"""
+import datetime
+import os
+
+import numpy as np
+
+RAYS, STEPS, RES, LOG2T, MAXRES = 512, 96, 32, 15, 512
+
+
+def small_problem():
+    import nerf_b200
+    ds = nerf_b200.make_scene(kind=0, seed=0, n_views=8, width=48, height=48, fov=0.69, radius=3.0)
+    cfg = nerf_b200.training_config(rays=RAYS, steps=STEPS, warmup=4, update_interval=2, cells_per_update=RES ** 3 // 2)
+    return ds, cfg
+
+
+def oracle_context(ds, cfg, rank, world):
+    import nerf_b200
+    from oracle import oracle
+    desc, imgs, cams = nerf_b200.create_desc(ds, grid_res=RES, max_sample_steps=RAYS * STEPS, max_batch_rays=4 * RAYS)
+    oc = oracle.Context(desc, oracle.options(log2_hashmap_size=LOG2T, max_resolution=MAXRES, dp_rank=rank,
+                                             dp_world=world, n_threads=4), imgs, cams)
+    oc._desc_keep = (desc, imgs, cams)
+    oc.configure(cfg)
+    return oc
+
+
+def _init(rank, world, port):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    return dist
+
+
+def oracle_rank(rank, world, port, steps, q):
+    """One rank of oracle data-parallel training with a gloo all-reduce."""
+    try:
+        import torch
+        dist = _init(rank, world, port)
+        ds, cfg = small_problem()
+        oc = oracle_context(ds, cfg, rank, world)
+        for _ in range(steps):
+            oc.step_grads()
+            grad = torch.from_numpy(oc.params()[4].copy())
+            loss_sum, active = oc.loss()
+            loss = torch.tensor([loss_sum], dtype=torch.float32)
+            dist.all_reduce(grad)
+            dist.all_reduce(loss)
+            oc.set_grads(grad.numpy(), float(loss[0]), active)
+            oc.step_apply()
+        q.put((rank, oc.params()[0], oc.batch()["counts"], oc.stats().loss))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent instead of hanging it
+        q.put((rank, repr(e), None, None))
+
+
+def serial_emulation(world, steps):
+    """The same data-parallel training with all ranks in this process."""
+    ds, cfg = small_problem()
+    ocs = [oracle_context(ds, cfg, r, world) for r in range(world)]
+    for _ in range(steps):
+        for oc in ocs:
+            oc.step_grads()
+        grad = ocs[0].params()[4].copy()
+        loss = np.float32(ocs[0].loss()[0])
+        for oc in ocs[1:]:
+            grad += oc.params()[4]
+            loss += np.float32(oc.loss()[0])
+        for oc in ocs:
+            oc.set_grads(grad, float(loss), oc.loss()[1])
+            oc.step_apply()
+    return [oc.params()[0] for oc in ocs], [oc.batch() for oc in ocs], [oc.params() for oc in ocs]
+
+
+def gpu_rank(rank, world, port, steps, q):
+    """One rank of GPU data-parallel training (NCCL inside the step)."""
+    try:
+        import torch
+        import nerf_b200
+        dist = _init(rank, world, port)
+        torch.cuda.set_device(rank)
+        ds, cfg = small_problem()
+        ctx = nerf_b200.Context(ds, grid_res=RES, max_sample_steps=RAYS * STEPS, max_batch_rays=4 * RAYS,
+                                options=nerf_b200.default_options(log2_hashmap_size=LOG2T, max_resolution=MAXRES))
+        uid = [nerf_b200.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        ctx.dp_init(rank, world, uid[0])
+        ctx.configure(cfg)
+        for _ in range(steps):
+            ctx.train_step()
+        master, _, m, v = ctx.params()
+        b = ctx.batch()
+        q.put((rank, master, m, b["counts"], ctx.stats().loss))
+        ctx.close()
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        q.put((rank, repr(e), None, None, None))
