@@ -177,8 +177,10 @@ __device__ __forceinline__ void adam_chunk(const OptimArgs& a, uint64_t q, uint6
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         const float gk = __fmul_rn(__fmul_rn(c.g[k], s.inv_loss_scale), s.grad_scale);
-        const float mi = __fadd_rn(__fmul_rn(b1, mm[k]), __fmul_rn(omb1, gk));
-        const float vi = __fadd_rn(__fmul_rn(b2, vv[k]), __fmul_rn(__fmul_rn(omb2, gk), gk));
+        // b*m + (1-b)*g with the first product fused, as the reference's
+        // compiler contracts it (backend-cuda.cu:1546-1547).
+        const float mi = __fmaf_rn(b1, mm[k], __fmul_rn(omb1, gk));
+        const float vi = __fmaf_rn(b2, vv[k], __fmul_rn(__fmul_rn(omb2, gk), gk));
         const float num = __fmul_rn(s.learning_rate, __fmul_rn(mi, s.inv_bias_correction1));
         const float den = __fadd_rn(__fsqrt_rn(__fmul_rn(vi, s.inv_bias_correction2)), a.tc.eps);
         w[k] = __fsub_rn(w[k], __fdiv_rn(num, den));

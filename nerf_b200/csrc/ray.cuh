@@ -20,7 +20,9 @@ struct AabbConsts {
 // Camera ray through continuous pixel (px, py); py is measured from the top
 // row and flipped to H-1-py (reference backend-cuda.cu:373-390, 438-441).
 // cam: rows 0..2 of a row-major 4x4 camera-to-world matrix.  The direction is
-// normalised with a correctly rounded 1/sqrt.
+// normalised with a correctly rounded 1/sqrt.  Sums of products a*b + c*d
+// (+ e*f) are evaluated as fma(e, f, fma(a, b, c*d)), the contraction the
+// reference's compiler applies to the same expressions.
 NB_DEV bool camera_ray(const float* cam, float fx, float fy, float cx, float cy, float height, float px, float py, Ray& r) {
     const float pyf = __fsub_rn(__fsub_rn(height, 1.0f), py);
     r.o[0] = cam[3];
@@ -30,8 +32,8 @@ NB_DEV bool camera_ray(const float* cam, float fx, float fy, float cx, float cy,
     const float dcy = __fdiv_rn(__fsub_rn(pyf, cy), fy);
 #pragma unroll
     for (int k = 0; k < 3; ++k)
-        r.d[k] = __fmaf_rn(cam[4 * k + 2], -1.0f, __fmaf_rn(cam[4 * k + 1], dcy, __fmul_rn(cam[4 * k + 0], dcx)));
-    const float len2 = __fmaf_rn(r.d[2], r.d[2], __fmaf_rn(r.d[1], r.d[1], __fmul_rn(r.d[0], r.d[0])));
+        r.d[k] = __fmaf_rn(cam[4 * k + 2], -1.0f, __fmaf_rn(cam[4 * k + 0], dcx, __fmul_rn(cam[4 * k + 1], dcy)));
+    const float len2 = __fmaf_rn(r.d[2], r.d[2], __fmaf_rn(r.d[0], r.d[0], __fmul_rn(r.d[1], r.d[1])));
     if (len2 <= 1e-16f) return false;
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(len2));
 #pragma unroll

@@ -284,9 +284,9 @@ __device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom
         const float s10 = __fmul_rn(static_cast<float>((q10 >> (8 * ch)) & 255u), inv255);
         const float s01 = __fmul_rn(static_cast<float>((q01 >> (8 * ch)) & 255u), inv255);
         const float s11 = __fmul_rn(static_cast<float>((q11 >> (8 * ch)) & 255u), inv255);
-        const float ta = __fmaf_rn(s10, tx, __fmul_rn(s00, omtx));
-        const float tb = __fmaf_rn(s11, tx, __fmul_rn(s01, omtx));
-        v[ch] = __fmaf_rn(tb, ty, __fmul_rn(ta, omty));
+        const float ta = __fmaf_rn(s00, omtx, __fmul_rn(s10, tx));
+        const float tb = __fmaf_rn(s01, omtx, __fmul_rn(s11, tx));
+        v[ch] = __fmaf_rn(ta, omty, __fmul_rn(tb, ty));
     }
     RayRecord rec;
     rec.dir[0] = g.d[0];

@@ -153,6 +153,10 @@ uint64_t oracle_ctx_param_count(void* ctx, uint64_t* n_grid, uint64_t* n_mlp);
 int oracle_ctx_get_params(void* ctx, float* master, uint16_t* p16, float* m, float* v, float* grad);
 int oracle_ctx_set_params(void* ctx, const float* master);
 int oracle_ctx_set_grads(void* ctx, const float* grad, float loss_sum, uint32_t active_rays);
+/* World positions (x, y, z) of the update_count cells queried by an
+ * occupancy refresh at this frame. */
+void oracle_occupancy_cells(uint32_t frame, uint32_t update_count, uint32_t cell_count, uint32_t grid_res, const float* mn,
+                            const float* mx, float* out_xyz);
 /* Loss sum (already normalised) and kept rays of the pending step. */
 int oracle_ctx_get_loss(void* ctx, float* loss_sum, uint32_t* active_rays);
 int oracle_ctx_get_occupancy(void* ctx, float* density, uint32_t* bitfield);

@@ -76,6 +76,7 @@ _PROTOS = {
     "oracle_ctx_set_params": (C.c_int, [P, P]),
     "oracle_ctx_set_grads": (C.c_int, [P, P, F32, U32]),
     "oracle_ctx_get_loss": (C.c_int, [P, P, P]),
+    "oracle_occupancy_cells": (None, [U32, U32, U32, U32, P, P, P]),
     "oracle_ctx_get_occupancy": (C.c_int, [P, P, P]),
     "oracle_ctx_set_occupancy": (C.c_int, [P, P, P]),
     "oracle_ctx_set_frame": (C.c_int, [P, U32]),
@@ -197,6 +198,14 @@ def adam(master, p16, grad, m, v, b1, b2, eps, s: AdamScalars):
 def occupancy_update(density, bits, sigma, cell_count, update_count, frame, mode, decay, threshold):
     lib().oracle_occupancy_update(ptr(density), ptr(bits), ptr(sigma), cell_count, update_count, frame, mode, decay,
                                   threshold)
+
+
+def occupancy_cells(frame, update_count, cell_count, grid_res, aabb_min, aabb_max):
+    """World positions of the cells an occupancy refresh queries at this frame."""
+    out = np.zeros((update_count, 3), np.float32)
+    mn, mx = np.asarray(aabb_min, np.float32), np.asarray(aabb_max, np.float32)
+    lib().oracle_occupancy_cells(frame, update_count, cell_count, grid_res, ptr(mn), ptr(mx), ptr(out))
+    return out
 
 
 def options(n_levels=16, log2_hashmap_size=19, base_resolution=16, max_resolution=2048, hash_init_scale=1e-4,

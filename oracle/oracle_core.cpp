@@ -415,8 +415,10 @@ void adam_range(float* master, uint16_t* p16, const float* grad, float* m, float
     if (s.skip_update) return;
     for (uint64_t i = begin; i < end; ++i) {
         const float g = grad[i] * s.inv_loss_scale * s.grad_scale;
-        const float mi = beta1 * m[i] + (1.0f - beta1) * g;
-        const float vi = beta2 * v[i] + (1.0f - beta2) * g * g;
+        // b*m + (1-b)*g with the first product fused, as the reference's
+        // compiler contracts it (backend-cuda.cu:1546-1547).
+        const float mi = std::fmaf(beta1, m[i], (1.0f - beta1) * g);
+        const float vi = std::fmaf(beta2, v[i], (1.0f - beta2) * g * g);
         const float step = s.learning_rate * (mi * s.inv_bias_correction1) / (std::sqrt(vi * s.inv_bias_correction2) + eps);
         const float w = master[i] - step;
         m[i] = mi;

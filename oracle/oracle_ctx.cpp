@@ -52,8 +52,10 @@ bool ray_dir(const float* cam, float fx, float fy, float cx, float cy, float px,
     const float dcx = (px - cx) / fx;
     const float dcy = (pyf - cy) / fy;
     const float dcz = -1.0f;
-    for (int k = 0; k < 3; ++k) d[k] = std::fmaf(cam[4 * k + 2], dcz, std::fmaf(cam[4 * k + 1], dcy, cam[4 * k + 0] * dcx));
-    const float len2 = std::fmaf(d[2], d[2], std::fmaf(d[1], d[1], d[0] * d[0]));
+    // a*b + c*d + e*f evaluated as fma(e, f, fma(a, b, c*d)): the contraction
+    // the reference's compiler applies (pinned against its kernel outputs).
+    for (int k = 0; k < 3; ++k) d[k] = std::fmaf(cam[4 * k + 2], dcz, std::fmaf(cam[4 * k + 0], dcx, cam[4 * k + 1] * dcy));
+    const float len2 = std::fmaf(d[2], d[2], std::fmaf(d[0], d[0], d[1] * d[1]));
     if (len2 <= 1e-16f) return false;
     const float inv = 1.0f / std::sqrt(len2);
     for (int k = 0; k < 3; ++k) d[k] = d[k] * inv;
@@ -225,25 +227,33 @@ void occupancy_apply(float* density, uint32_t* bits, const float* sig, uint32_t 
         if (density[c] > threshold) bits[c >> 5] |= 1u << (c & 31u);
 }
 
+// World position of the k-th queried cell of an occupancy refresh: cells
+// are visited round-robin from frame * update_count mod C, the query point is
+// the cell centre (reference backend-cuda.cu:1575-1616).
+void occupancy_cell_center(uint32_t frame, uint32_t k, uint32_t update_count, uint32_t cell_count, uint32_t R,
+                           const float mn[3], const float mx[3], float c[3]) {
+    const uint32_t start = static_cast<uint32_t>(static_cast<uint64_t>(frame) * update_count % cell_count);
+    const uint32_t cell = static_cast<uint32_t>((static_cast<uint64_t>(start) + k) % cell_count);
+    const uint32_t z = cell / (R * R), rem = cell - z * R * R, y = rem / R, x = rem - y * R;
+    const uint32_t ci[3] = {x, y, z};
+    for (int d = 0; d < 3; ++d) {
+        const float step = (mx[d] - mn[d]) / static_cast<float>(R);
+        c[d] = std::fmaf(static_cast<float>(ci[d]) + 0.5f, step, mn[d]);
+    }
+}
+
 // Densities of the query window: cell centres through the hash grid and the
 // density MLP, sigma = exp(raw).
 void Ctx::occupancy_step(uint32_t mode) {
     std::vector<float> sig;
     if (mode == kOccRefresh) {
-        const uint32_t R = grid_res;
-        const uint32_t start = static_cast<uint32_t>(static_cast<uint64_t>(frame) * update_count % cell_count);
-        float step[3];
-        for (int k = 0; k < 3; ++k) step[k] = (mx[k] - mn[k]) / static_cast<float>(R);
         sig.resize(update_count);
         float W[kMlpParams];
         for (uint32_t i = 0; i < kMlpParams; ++i) W[i] = h2f(p16[n_grid + i]);
         parallel_for(update_count, opt.n_threads, [&](uint64_t b, uint64_t e, uint32_t) {
             for (uint64_t k = b; k < e; ++k) {
-                const uint32_t cell = static_cast<uint32_t>((start + k) % cell_count);
-                const uint32_t z = cell / (R * R), rem = cell - z * R * R, y = rem / R, x = rem - y * R;
-                const float c[3] = {std::fmaf(static_cast<float>(x) + 0.5f, step[0], mn[0]),
-                                    std::fmaf(static_cast<float>(y) + 0.5f, step[1], mn[1]),
-                                    std::fmaf(static_cast<float>(z) + 0.5f, step[2], mn[2])};
+                float c[3];
+                occupancy_cell_center(frame, static_cast<uint32_t>(k), update_count, cell_count, grid_res, mn, mx, c);
                 float u[3];
                 to_unit(c, u);
                 uint16_t feat[64];
@@ -342,9 +352,9 @@ void Ctx::sample_batch(uint32_t camera) {
             auto px = [&](int x, int y, int ch) { return static_cast<float>(img[(static_cast<uint64_t>(y) * W + x) * 4u + ch]) * inv255; };
             float v[4];
             for (int ch = 0; ch < 4; ++ch) {
-                const float a = std::fmaf(px(x1, y0, ch), tx, px(x0, y0, ch) * (1.0f - tx));
-                const float bb = std::fmaf(px(x1, y1, ch), tx, px(x0, y1, ch) * (1.0f - tx));
-                v[ch] = std::fmaf(bb, ty, a * (1.0f - ty));
+                const float a = std::fmaf(px(x0, y0, ch), 1.0f - tx, px(x1, y0, ch) * tx);
+                const float bb = std::fmaf(px(x0, y1, ch), 1.0f - tx, px(x1, y1, ch) * tx);
+                v[ch] = std::fmaf(a, 1.0f - ty, bb * ty);
             }
             for (int ch = 0; ch < 3; ++ch) k_gt[4 * k + ch] = std::fmaf(v[ch], v[3], bg[ch] * (1.0f - v[3]));
             k_gt[4 * k + 3] = v[3];
@@ -597,6 +607,11 @@ int oracle_ctx_set_grads(void* ctx, const float* grad, float loss_sum, uint32_t 
     c->loss_sum = loss_sum;
     c->active = active_rays;
     return NERF_STATUS_OK;
+}
+
+void oracle_occupancy_cells(uint32_t frame, uint32_t update_count, uint32_t cell_count, uint32_t grid_res, const float* mn,
+                            const float* mx, float* out_xyz) {
+    for (uint32_t k = 0; k < update_count; ++k) occupancy_cell_center(frame, k, update_count, cell_count, grid_res, mn, mx, out_xyz + 3ull * k);
 }
 
 int oracle_ctx_get_loss(void* ctx, float* loss_sum, uint32_t* active_rays) {
