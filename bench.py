@@ -220,6 +220,14 @@ def run_ours(args):
     prof /= max(1, n_prof)
     mean_samples = prof_samples / max(1, n_prof)
     kernels = kernel_table(ctx, prof, mean_samples)
+    l2 = l2_peaks(lib, stream)
+    for k in kernels:  # L2-bound field kernels against the measured L2 peaks
+        if k["kernel"] == "field_forward":
+            k["l2_gather_gbs"] = mean_samples * 128 * 4 / (k["ms"] / 1e3) / 1e9
+            k["l2_frac"] = k["l2_gather_gbs"] / l2["read_gbs"]
+        if k["kernel"] == "field_backward":
+            k["corner_updates_g_per_s"] = mean_samples * 128 / (k["ms"] / 1e3) / 1e9
+            k["l2_red_frac"] = k["corner_updates_g_per_s"] / l2["red_f16x2_gops"]
 
     render = None
     if not args.skip_render:
@@ -251,6 +259,7 @@ def run_ours(args):
             "e2e": e2e,
             "gpu_launches": KERNELS_PER_STEP * args.steps,
             "roofline": roofline(dom, hbm, src),
+            "l2": l2,
             "kernels": kernels,
             "render": render,
             "cpu_baseline": cpu,
@@ -289,6 +298,44 @@ def kernel_table(ctx, prof_ms, samples):
         b = per.get(name, 0)
         out.append({"kernel": name, "ms": float(ms), "bytes": int(b), "gbs": (b / (ms / 1e3) / 1e9) if ms > 0 else 0.0})
     return out
+
+
+def l2_peaks(lib, stream):
+    """L2 peaks of this GPU from the library's probes: 16-byte read bandwidth of
+    an L2-resident 64 MB buffer, and f16x2 / v2.f16x2 reduction rates at hashed
+    addresses of a 32 MB buffer (the shape of the hash-table scatter)."""
+    import ctypes as C
+
+    import torch
+    h = C.c_void_p(stream.cuda_stream)
+    sink = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    res = {}
+
+    def timed(fn, reps=5):
+        fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    buf = torch.zeros(64 << 20, dtype=torch.uint8, device="cuda")
+    passes = 16
+    t = timed(lambda: lib.nerf_b200_probe_l2_read(buf.data_ptr(), buf.numel(), passes, sink.data_ptr(), h))
+    res["read_gbs"] = buf.numel() * passes / t / 1e9
+    del buf
+    words = 1 << 23
+    rb = torch.zeros(words, dtype=torch.int32, device="cuda")
+    ops = C.c_uint64()
+    for vec, key in ((0, "red_f16x2_gops"), (1, "red_v2_f16x2_gops")):
+        t = timed(lambda: lib.nerf_b200_probe_l2_red(rb.data_ptr(), words, 64, vec, C.byref(ops), h))
+        res[key] = ops.value / t / 1e9
+    res["note"] = ("probes: 64 MB L2-resident buffer, 16 sweeps of 16-byte loads; f16x2 reductions at hashed word "
+                   "addresses of a 32 MB buffer (v2: 8-byte form), 64 per thread over 8 blocks x 256 threads per SM")
+    return res
 
 
 def ctx_partials(ctx):

@@ -250,7 +250,7 @@ __device__ __forceinline__ void world_to_unit(const FieldArgs& a, const float pw
     for (int k = 0; k < 3; ++k) u[k] = clamp01(__fdiv_rn(__fsub_rn(pw[k], a.aabb_min[k]), a.aabb_size[k]));
 }
 
-__device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool valid, uint32_t* row_tail = nullptr) {
+__device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool valid) {
     float sh[16];
     if (valid) {
         sh4(d[0], d[1], d[2], sh);
@@ -264,10 +264,6 @@ __device__ __forceinline__ void write_sh(__half* xc_row, const float d[3], bool 
     uint4* dst = reinterpret_cast<uint4*>(xc_row + 16u);
     dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
     dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    if (row_tail) {
-        reinterpret_cast<uint4*>(row_tail)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        reinterpret_cast<uint4*>(row_tail)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
 }
 
 // Training forward: copies of the next tile's pos+dt and ray ids.
@@ -323,47 +319,55 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
         }
     }
     s.pos[tid] = make_float4(u[0], u[1], u[2], 0.0f);
-    // Training rows carry SH and unit position for the backward pass.
-    uint32_t* tail = nullptr;
-    if (mode == kFieldTrain && valid && a.feat != nullptr) {
-        uint32_t* row = static_cast<uint32_t*>(a.feat) + static_cast<unsigned long long>(r) * kTrainRowU32;
-        tail = row + 16u;
-        reinterpret_cast<float4*>(row + 24u)[0] = make_float4(u[0], u[1], u[2], 0.0f);
-    }
-    write_sh(s.xc + tid * kS32, d, valid && mode != kFieldOccupancy, tail);
+    write_sh(s.xc + tid * kS32, d, valid && mode != kFieldOccupancy);
 }
 
-// Hash-grid encode of a tile: 64 rows x 16 levels over 128 threads; each
-// thread keeps one level and walks 8 rows two at a time.
-__device__ __forceinline__ void encode_tile(const FieldArgs& a, const Smem& s, uint32_t row0, uint32_t n, bool store_global,
-                                            uint32_t row_u32) {
-    const uint32_t tid = threadIdx.x;
-    const uint32_t l = tid % kL;
-    const LevelParams lp = s.lv[l];
-    const uint32_t* P = static_cast<const uint32_t*>(a.params16);
-    uint32_t* gfeat = static_cast<uint32_t*>(a.feat);
+// Hash encode of a 64-row tile into feat[64][40] (level l in columns 2l,
+// 2l+1).  Warp w takes levels w, w+4, w+8, w+12 and lane j rows j and j+32,
+// so one gather instruction reads one level for 32 consecutive rows: on all
+// but the finest levels consecutive samples of a ray (or neighbouring pixels
+// of a render tile) share cells, and their loads fall into few sectors.
+// ok(row, pos) says whether a row is live.
+template <class Ok>
+__device__ __forceinline__ void encode_rows(const uint32_t* __restrict__ P, const LevelParams* lv, uint32_t hash_mask,
+                                            const float4* pos, __half* feat, Ok ok) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t ra = lane, rb = lane + 32u;
+    const float4 pa4 = pos[ra], pb4 = pos[rb];
+    const float pa[3] = {pa4.x, pa4.y, pa4.z}, pb[3] = {pb4.x, pb4.y, pb4.z};
+    const bool oka = ok(ra, pa4), okb = ok(rb, pb4);
 #pragma unroll 1
-    for (uint32_t j = 0; j < kRows * kL / kThreads; j += 2) {
-        const uint32_t ra = tid / kL + j * (kThreads / kL);
-        const uint32_t rb = ra + kThreads / kL;
-        const float4 pa4 = s.pos[ra], pb4 = s.pos[rb];
-        const float pa[3] = {pa4.x, pa4.y, pa4.z}, pb[3] = {pb4.x, pb4.y, pb4.z};
+    for (uint32_t i = 0; i < kL / 4u; ++i) {
+        const uint32_t l = warp + 4u * i;
+        const LevelParams lp = lv[l];
         uint32_t va = 0u, vb = 0u;
-        const bool oka = row0 + ra < n, okb = row0 + rb < n;
         if (oka && okb) {
-            level_forward2(P, pa, lp, pb, lp, a.lt.hash_mask, va, vb);
+            level_forward2(P, pa, lp, pb, lp, hash_mask, va, vb);
         } else {
-            if (oka) va = level_forward(P, pa, lp, a.lt.hash_mask);
-            if (okb) vb = level_forward(P, pb, lp, a.lt.hash_mask);
+            if (oka) va = level_forward(P, pa, lp, hash_mask);
+            if (okb) vb = level_forward(P, pb, lp, hash_mask);
         }
-        *reinterpret_cast<uint32_t*>(s.feat + ra * kS32 + 2u * l) = va;
-        *reinterpret_cast<uint32_t*>(s.feat + rb * kS32 + 2u * l) = vb;
-        if (store_global) {
-            if (oka) gfeat[static_cast<unsigned long long>(row0 + ra) * row_u32 + l] = va;
-            if (okb) gfeat[static_cast<unsigned long long>(row0 + rb) * row_u32 + l] = vb;
-        }
+        *reinterpret_cast<uint32_t*>(feat + ra * kS32 + 2u * l) = va;
+        *reinterpret_cast<uint32_t*>(feat + rb * kS32 + 2u * l) = vb;
     }
 }
+
+// Rows of a tile to global memory in 16-byte pieces, one row after another:
+// training rows are features | SH | unit position (112 bytes), kernel-level
+// rows features only (64 bytes).
+__device__ __forceinline__ void store_rows(const FieldArgs& a, const Smem& s, int mode, uint32_t row0, uint32_t n) {
+    const uint32_t q_per_row = mode == kFieldTrain ? kTrainRowU32 / 4u : kFeatRowU32 / 4u;
+    uint4* dst = static_cast<uint4*>(a.feat);
+    for (uint32_t c = threadIdx.x; c < kRows * q_per_row; c += kThreads) {
+        const uint32_t r = c / q_per_row, q = c - r * q_per_row;
+        if (row0 + r >= n) continue;
+        const uint4 v = q < 4u ? *reinterpret_cast<const uint4*>(s.feat + r * kS32 + 8u * q)
+                               : (q < 6u ? *reinterpret_cast<const uint4*>(s.xc + r * kS32 + 16u + 8u * (q - 4u))
+                                         : *reinterpret_cast<const uint4*>(s.pos + r));
+        dst[static_cast<unsigned long long>(row0 + r) * q_per_row + q] = v;
+    }
+}
+
 
 __device__ __forceinline__ void load_levels(const LevelTable& lt, LevelParams* lv) {
     if (threadIdx.x < lt.n_levels) {
@@ -428,9 +432,10 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
         __syncthreads();  // this tile's stage is visible; the previous tile is done with shared memory
         load_rows(a, mode, s, &cur, row0, n);
         __syncthreads();
-        encode_tile(a, s, row0, n, mode != kFieldOccupancy && a.feat != nullptr,
-                    mode == kFieldTrain ? kTrainRowU32 : kFeatRowU32);
+        encode_rows(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
+                    [&](uint32_t r, const float4&) { return row0 + r < n; });
         __syncthreads();
+        if (mode != kFieldOccupancy && a.feat != nullptr) store_rows(a, s, mode, row0, n);
         const uint32_t wrow = warp * 16u;
         Chain c;
         forward_density(s.w, s.feat, wrow, lane, c);
@@ -867,26 +872,8 @@ __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
         }
         if (!__syncthreads_or(has_row)) break;
         // Encode the tile's live rows.
-        {
-            const uint32_t l = tid % kL;
-            const LevelParams lp = s.lv[l];
-            const uint32_t* P = static_cast<const uint32_t*>(a.params16);
-#pragma unroll 1
-            for (uint32_t j = 0; j < kRows * kL / kThreads; j += 2) {
-                const uint32_t ra = tid / kL + j * (kThreads / kL), rb = ra + kThreads / kL;
-                const float4 pa4 = s.pos[ra], pb4 = s.pos[rb];
-                const float pa[3] = {pa4.x, pa4.y, pa4.z}, pb[3] = {pb4.x, pb4.y, pb4.z};
-                uint32_t va = 0u, vb = 0u;
-                if (pa4.w > 0.0f && pb4.w > 0.0f) {
-                    level_forward2(P, pa, lp, pb, lp, a.lt.hash_mask, va, vb);
-                } else {
-                    if (pa4.w > 0.0f) va = level_forward(P, pa, lp, a.lt.hash_mask);
-                    if (pb4.w > 0.0f) vb = level_forward(P, pb, lp, a.lt.hash_mask);
-                }
-                *reinterpret_cast<uint32_t*>(s.feat + ra * kS32 + 2u * l) = va;
-                *reinterpret_cast<uint32_t*>(s.feat + rb * kS32 + 2u * l) = vb;
-            }
-        }
+        encode_rows(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
+                    [](uint32_t, const float4& p) { return p.w > 0.0f; });
         __syncthreads();
         {
             const uint32_t wrow = warp * 16u;
