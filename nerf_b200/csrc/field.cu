@@ -560,11 +560,11 @@ __device__ __forceinline__ void scatter_runs(uint32_t* G, const LevelParams lp, 
         }
     }
     if (!(ok && head)) return;
+    uint32_t e[8];
+    corner_entries(i, lp, hash_mask, e);
 #pragma unroll
-    for (uint32_t c = 0; c < 8u; c += 2u) {
-        const uint32_t ea = corner_entry(i, c, lp, hash_mask), eb = corner_entry(i, c + 1u, lp, hash_mask);
-        red_pair(G, ea, eb, *reinterpret_cast<const uint32_t*>(&v[c]), *reinterpret_cast<const uint32_t*>(&v[c + 1]));
-    }
+    for (uint32_t c = 0; c < 8u; c += 2u)
+        red_pair(G, e[c], e[c + 1], *reinterpret_cast<const uint32_t*>(&v[c]), *reinterpret_cast<const uint32_t*>(&v[c + 1]));
 }
 
 __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs a, const int mode) {

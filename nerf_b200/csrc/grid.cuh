@@ -37,30 +37,46 @@ NB_DEV void level_cell(const float p[3], const LevelParams lp, uint32_t i[3], fl
         i[d] = static_cast<uint32_t>(ii);
     }
 }
-// Table entry of corner c of cell i.
-NB_DEV uint32_t corner_entry(const uint32_t i[3], uint32_t c, const LevelParams lp, uint32_t hash_mask) {
-    const uint32_t cx = i[0] + (c & 1u), cy = i[1] + ((c >> 1) & 1u), cz = i[2] + ((c >> 2) & 1u);
-    const uint32_t e = lp.dense ? cx + lp.res * (cy + lp.res * cz) : ((cx ^ (cy * 2654435761u) ^ (cz * 805459861u)) & hash_mask);
-    return lp.offset + e;
+// Table entries of all 8 corners of cell i.  The dense / hashed choice is
+// one branch (uniform across a warp when the warp works on one level), and
+// the per-axis terms are shared between corners: (y+1)*p = y*p + p mod 2^32.
+NB_DEV void corner_entries(const uint32_t i[3], const LevelParams lp, uint32_t hash_mask, uint32_t idx[8]) {
+    if (lp.dense) {
+        const uint32_t R = lp.res, RR = R * R;
+        const uint32_t b = lp.offset + i[0] + R * (i[1] + R * i[2]);
+        idx[0] = b;
+        idx[1] = b + 1u;
+        idx[2] = b + R;
+        idx[3] = b + R + 1u;
+        idx[4] = b + RR;
+        idx[5] = b + RR + 1u;
+        idx[6] = b + RR + R;
+        idx[7] = b + RR + R + 1u;
+    } else {
+        const uint32_t x0 = i[0], x1 = i[0] + 1u;
+        const uint32_t y0 = i[1] * 2654435761u, y1 = y0 + 2654435761u;
+        const uint32_t z0 = i[2] * 805459861u, z1 = z0 + 805459861u;
+        const uint32_t yz[4] = {y0 ^ z0, y1 ^ z0, y0 ^ z1, y1 ^ z1};
+#pragma unroll
+        for (uint32_t k = 0; k < 4u; ++k) {
+            idx[2 * k] = lp.offset + ((x0 ^ yz[k]) & hash_mask);
+            idx[2 * k + 1] = lp.offset + ((x1 ^ yz[k]) & hash_mask);
+        }
+    }
 }
-// Trilinear weight of corner c.
+// Trilinear weight of corner c, ((wx*wy)*wz) with the x-y products shared.
 NB_DEV void corner_weights(const float f[3], float w[8]) {
     const float g0[3] = {__fsub_rn(1.0f, f[0]), __fsub_rn(1.0f, f[1]), __fsub_rn(1.0f, f[2])};
+    const float xy[4] = {__fmul_rn(g0[0], g0[1]), __fmul_rn(f[0], g0[1]), __fmul_rn(g0[0], f[1]), __fmul_rn(f[0], f[1])};
 #pragma unroll
-    for (uint32_t c = 0; c < 8u; ++c) {
-        const float wx = (c & 1u) ? f[0] : g0[0];
-        const float wy = (c & 2u) ? f[1] : g0[1];
-        const float wz = (c & 4u) ? f[2] : g0[2];
-        w[c] = __fmul_rn(__fmul_rn(wx, wy), wz);
-    }
+    for (uint32_t c = 0; c < 8u; ++c) w[c] = __fmul_rn(xy[c & 3u], (c & 4u) ? f[2] : g0[2]);
 }
 
 NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_mask, uint32_t idx[8], float w[8]) {
     uint32_t i[3];
     float f[3];
     level_cell(p, lp, i, f);
-#pragma unroll
-    for (uint32_t c = 0; c < 8u; ++c) idx[c] = corner_entry(i, c, lp, hash_mask);
+    corner_entries(i, lp, hash_mask, idx);
     corner_weights(f, w);
 }
 
