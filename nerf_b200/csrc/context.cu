@@ -228,6 +228,7 @@ struct Context {
     void* feat = nullptr;
     float4* raw = nullptr;
     float4* dout = nullptr;
+    void* dfeat = nullptr;  // feature gradients of the training backward (fp16 x 32 per sample)
     float* partials = nullptr;
     float* occ_sigma = nullptr;
     uint32_t n_partials = 0, fwd_blocks = 0;
@@ -489,7 +490,7 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     const uint64_t o_bs = batch.add(t.max_rays * 4ull), o_ba = batch.add(t.max_rays * 4ull);
     const uint64_t o_rays = batch.add(t.max_rays * sizeof(RayRecord)), o_ri = batch.add(t.max_rays * 4ull);
     const uint64_t o_pos = batch.add(cap * 16u), o_sr = batch.add(cap * 4u), o_feat = batch.add(cap * 112u);
-    const uint64_t o_raw = batch.add(cap * 16u), o_dout = batch.add(cap * 16u);
+    const uint64_t o_raw = batch.add(cap * 16u), o_dout = batch.add(cap * 16u), o_dfeat = batch.add(cap * 64u);
     const uint64_t o_part = batch.add(static_cast<uint64_t>(n_partials) * kMlpParams * 4u);
     const uint64_t o_sig = batch.add(std::max<uint32_t>(t.update_count, 1u) * 4ull);
     if (batch.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
@@ -506,6 +507,7 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     feat = batch.at<void>(o_feat);
     raw = batch.at<float4>(o_raw);
     dout = batch.at<float4>(o_dout);
+    dfeat = batch.at<void>(o_dfeat);
     partials = batch.at<float>(o_part);
     occ_sigma = batch.at<float>(o_sig);
     NB_TRY(cudaMemsetAsync(batch.base, 0, batch.size, stream));
@@ -589,6 +591,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     fa.dout = dout;
     fa.grid_grad = grid_grad;
     fa.partials = partials;
+    fa.dfeat = dfeat;
 
     CompositeArgs ca{};
     ca.rays = rays;
@@ -1088,6 +1091,7 @@ NERF_API NerfStatus nerf_load_network_weights(void* context, const NerfCheckpoin
     NB_TRY(cudaMemcpyAsync(c->state, &st, sizeof(st), cudaMemcpyHostToDevice, c->stream));
     NB_TRY(cudaMemsetAsync(c->density, 0, static_cast<uint64_t>(c->words) * 32u * 4u, c->stream));
     NB_TRY(cudaMemsetAsync(c->bitfield, 0, c->words * 4ull, c->stream));
+    if (c->configured) NB_TRY(nb::launch_march(c->sampler_args(), c->stream));  // the step state restarted at frame 0
     NB_TRY(cudaStreamSynchronize(c->stream));
     c->occupancy_valid = false;
     c->host_generation = 0;

@@ -535,27 +535,30 @@ __device__ __forceinline__ void bwd_prefetch(const FieldArgs& a, int mode, const
 // less contention on the hot entries of coarse levels.  Rows of levels whose
 // cell coordinates do not pack into 30 bits (more than 1024 vertices per
 // axis) never merge.
-__device__ __forceinline__ void scatter_runs(uint32_t* G, const LevelParams lp, uint32_t hash_mask, const float p[3], bool ok,
-                                             float d0, float d1, uint32_t r, uint32_t lane) {
+template <uint32_t W>
+__device__ __forceinline__ void scatter_runs_w(uint32_t* G, const LevelParams lp, uint32_t hash_mask, const float p[3], bool ok,
+                                               float d0, float d1, uint32_t r, uint32_t lane) {
+    static_assert(W == 16u || W == 32u, "run width");
+    constexpr uint32_t kFull = W == 32u ? 0xFFFFFFFFu : 0xFFFFu;
     uint32_t i[3];
     float f[3], w[8];
     level_cell(p, lp, i, f);
     const uint32_t key = (ok && lp.res <= 1024u) ? (i[0] | (i[1] << 10) | (i[2] << 20)) : (0x80000000u | lane);
-    const uint32_t next = __shfl_down_sync(0xffffffffu, key, 1, 16);
-    const uint32_t ends = (__ballot_sync(0xffffffffu, r == 15u || next != key) >> (lane & 16u)) & 0xFFFFu;
-    const uint32_t end = static_cast<uint32_t>(__ffs(ends & (0xFFFFu << r))) - 1u;  // last row of this run
+    const uint32_t next = __shfl_down_sync(0xffffffffu, key, 1, W);
+    const uint32_t ends = (__ballot_sync(0xffffffffu, r == W - 1u || next != key) >> (lane & ~(W - 1u))) & kFull;
+    const uint32_t end = static_cast<uint32_t>(__ffs(ends & (kFull << r))) - 1u;  // last row of this run
     const bool head = r == 0u || ((ends >> (r - 1u)) & 1u);
     corner_weights(f, w);
     __half2 v[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) v[c] = __floats2half2_rn(w[c] * d0, w[c] * d1);
 #pragma unroll
-    for (uint32_t o = 1; o < 16u; o <<= 1) {
+    for (uint32_t o = 1; o < W; o <<= 1) {
         const bool take = r + o <= end;
         if (!__any_sync(0xffffffffu, take)) break;
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-            const __half2 x = __shfl_down_sync(0xffffffffu, v[c], o, 16);
+            const __half2 x = __shfl_down_sync(0xffffffffu, v[c], o, W);
             if (take) v[c] = __hadd2(v[c], x);
         }
     }
@@ -565,6 +568,49 @@ __device__ __forceinline__ void scatter_runs(uint32_t* G, const LevelParams lp, 
 #pragma unroll
     for (uint32_t c = 0; c < 8u; c += 2u)
         red_pair(G, e[c], e[c + 1], *reinterpret_cast<const uint32_t*>(&v[c]), *reinterpret_cast<const uint32_t*>(&v[c + 1]));
+}
+__device__ __forceinline__ void scatter_runs(uint32_t* G, const LevelParams lp, uint32_t hash_mask, const float p[3], bool ok,
+                                             float d0, float d1, uint32_t r, uint32_t lane) {
+    scatter_runs_w<16u>(G, lp, hash_mask, p, ok, d0, d1, r, lane);
+}
+
+// Hash-table scatter of the training backward: warp per 32 consecutive
+// rows (lane = row), all 16 levels, runs of rows in one cell merged over the
+// whole warp.  Inputs: the feature gradients (fp16 x 32 per row) and the unit
+// positions of the training rows.
+constexpr uint32_t kScatterThreads = 256;
+__global__ void __launch_bounds__(kScatterThreads) k_grid_scatter(const FieldArgs a) {
+    __shared__ LevelParams lv[kMaxLevels];
+    __shared__ uint32_t dsm[kScatterThreads / 32u][32][kL + 1];  // each lane's row of feature gradients
+    load_levels(a.lt, lv);
+    __syncthreads();
+    const uint32_t n = a.state->n_samples;
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t warps = gridDim.x * (kScatterThreads / 32u);
+    uint32_t* G = static_cast<uint32_t*>(a.grid_grad);
+    const uint4* rows = static_cast<const uint4*>(a.feat);
+    const uint4* dfe = static_cast<const uint4*>(a.dfeat);
+    for (uint32_t wb = blockIdx.x * (kScatterThreads / 32u) + (threadIdx.x >> 5); wb * 32u < n; wb += warps) {
+        const uint32_t r = wb * 32u + lane;
+        const bool ok = r < n;
+        const uint32_t rr = ok ? r : n - 1u;
+        const uint4 pq = rows[static_cast<unsigned long long>(rr) * (kTrainRowU32 / 4u) + 6u];
+        const float p[3] = {__uint_as_float(pq.x), __uint_as_float(pq.y), __uint_as_float(pq.z)};
+        uint32_t* mine = dsm[threadIdx.x >> 5][lane];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint4 q = dfe[static_cast<unsigned long long>(rr) * 4u + k];
+            mine[4 * k] = q.x;
+            mine[4 * k + 1] = q.y;
+            mine[4 * k + 2] = q.z;
+            mine[4 * k + 3] = q.w;
+        }
+#pragma unroll 1
+        for (uint32_t l = 0; l < kL; ++l) {
+            const float2 d = unpack_h2(mine[l]);
+            scatter_runs_w<32u>(G, lv[l], a.lt.hash_mask, p, ok, d.x, d.y, lane, lane);
+        }
+    }
 }
 
 __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs a, const int mode) {
@@ -651,10 +697,11 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
         }
         store_a(s.dyd, kS16, wrow, 0, dyd[0], lane);
 
-        // Hash-table scatter: dX (rounded to f16x2, the precision of the
-        // table's gradient) is transposed through shared memory to one row
-        // per lane of each half warp, half h taking levels h, h+2, ...; runs
-        // of rows in one cell are merged (scatter_runs).
+        // Hash-table gradient: dX (rounded to f16x2, the precision of the
+        // table's gradient) is transposed through shared memory to one row per
+        // lane.  Training: the rows go to dfeat for the scatter kernel.
+        // Direct: each half warp scatters its 16 rows, half h taking levels
+        // h, h+2, ..., with runs of rows in one cell merged (scatter_runs).
         __half2* runs = s.runs + warp * 16u * kRunStride;
 #pragma unroll
         for (uint32_t nt = 0; nt < 4u; ++nt) {
@@ -662,7 +709,16 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
             runs[(g + 8u) * kRunStride + 4u * nt + t] = __floats2half2_rn(dxd[nt][2], dxd[nt][3]);
         }
         __syncwarp();
-        {
+        if (mode == kFieldTrain) {
+            uint32_t* df = static_cast<uint32_t*>(a.dfeat);
+#pragma unroll
+            for (uint32_t k = 0; k < 8u; ++k) {
+                const uint32_t idx = lane + 32u * k, rr = idx >> 4, wd = idx & 15u;
+                if (row0 + wrow + rr < n)
+                    df[static_cast<unsigned long long>(row0 + wrow + rr) * 16u + wd] =
+                        *reinterpret_cast<const uint32_t*>(&runs[rr * kRunStride + wd]);
+            }
+        } else {
             const uint32_t r = lane & 15u, h = lane >> 4;
             const float4 p4 = cur.pos[wrow + r];
             const float p[3] = {p4.x, p4.y, p4.z};
@@ -952,7 +1008,14 @@ cudaError_t render_init_attributes() { return field_init_attributes(); }
 
 cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t blocks, cudaStream_t s) {
     if (blocks == 0u) return cudaErrorInvalidValue;
+    if (mode == kFieldTrain && a.dfeat == nullptr) return cudaErrorInvalidValue;
     k_field_backward<<<blocks, kThreads, kBwdSmem, s>>>(a, mode);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || mode != kFieldTrain) return e;
+    int dev = 0, sms = 148;
+    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+    k_grid_scatter<<<static_cast<uint32_t>(sms) * 8u, kScatterThreads, 0, s>>>(a);
     return cudaGetLastError();
 }
 

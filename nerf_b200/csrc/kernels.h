@@ -50,8 +50,11 @@ struct FieldArgs {
     const float4* dout;    // backward: loss-scaled d raw
     void* grid_grad;       // backward: fp16 entries x 2 (reduction target)
     float* partials;       // backward: [grid][kMlpParams] per-CTA weight gradients
+    void* dfeat;           // training backward: fp16 n x 32 feature gradients for the scatter kernel
 };
 cudaError_t launch_field_forward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
+// Training mode: MLP backward writing dfeat, then the hash-table scatter
+// kernel.  Direct mode: one fused kernel (MLP backward + scatter).
 cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
 uint32_t field_forward_blocks();
 uint32_t field_backward_blocks();
