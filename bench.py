@@ -54,8 +54,9 @@ WORKLOAD = ("config2 bounded training: 12 spheres/boxes, 100 views 800x800, hash
 
 # Kernel launches of one training step: occupancy query and update, the
 # sampler's bitfield / scan / write kernels, field forward, composite, field
-# backward, weight-gradient reduce, statistics, Adam and the next step's march.
-KERNELS_PER_STEP = 12
+# backward (MLP kernel + hash scatter kernel), weight-gradient reduce,
+# statistics, Adam and the next step's march.
+KERNELS_PER_STEP = 13
 
 
 def options(nb, **kw):
