@@ -87,12 +87,14 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
         self.proc = None
-        self.lines = []
+        self.lines = []  # (arrival time, csv line)
+        self.window = (0.0, float("inf"))
 
     def start(self):
+        """Starts sampling (nvidia-smi needs a moment to start: call before the warm-up steps)."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -101,11 +103,16 @@ class ClockSampler:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, t0, t1):
+        """The timed region, as host times; samples that arrive within it (plus one interval) count."""
+        self.window = (t0, t1 + 0.06)
 
     def stop(self):
         if not self.proc:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.1)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -113,7 +120,9 @@ class ClockSampler:
             self.proc.kill()
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in self.lines:
+        for ts, l in self.lines:
+            if not (self.window[0] <= ts <= self.window[1]):
+                continue
             parts = [x.strip() for x in l.split(",")]
             if len(parts) < 9:
                 continue
@@ -173,22 +182,24 @@ def run_ours(args):
     abi.check("stream", lib.nerf_b200_context_stream(ctx.handle, C.byref(sp)))
     stream = torch.cuda.ExternalStream(sp.value)
 
+    clocks = ClockSampler(local)
+    clocks.start()  # running well before the timed region
     for _ in range(args.pretrain):
         ctx.train_step()
     for _ in range(args.warmup):
         ctx.train_step()
     c0 = ctx.counters()
-    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks.start()
+    h0 = time.time()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
         ctx.train_step()
     e1.record(stream)
     torch.cuda.synchronize()
+    clocks.mark(h0, time.time())
     ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     if world > 1:
@@ -344,12 +355,20 @@ def ctx_partials(ctx):
     return int(abi.load().nerf_b200_field_backward_partial_floats()) // 10240
 
 
+# DRAM bytes (read + write) per launch from one ncu capture of this build
+# (profiles/field_kernels_adam_train_step_config2.md; cold-cache replay, so the
+# hash table and its gradient count as DRAM traffic).  field_backward is the
+# MLP kernel plus the hash scatter kernel.
+NCU_TRAFFIC = {"field_backward": 36.59e6 + 73.13e6, "field_forward": 31.67e6, "adam": 311.31e6}
+
+
 def roofline(dom, hbm, src):
     achieved = dom["gbs"]
     return {"kernel": dom["kernel"], "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-            "frac": achieved / hbm, "peak_source": src,
-            "traffic": None, "note": "achieved = algorithmic bytes per launch / mean CUDA-event launch time "
-                                     "(kernel-by-kernel step, same kernels as the graph); traffic from ncu in profiles/"}
+            "frac": achieved / hbm, "peak_source": src, "traffic": NCU_TRAFFIC.get(dom["kernel"]),
+            "note": "achieved = algorithmic bytes per launch / mean CUDA-event launch time (kernel-by-kernel step, "
+                    "same kernels as the graph); traffic = ncu DRAM bytes per launch; the field kernels are "
+                    "L2-bound, see the l2 object and the kernels' l2 fractions"}
 
 
 def run_render(nb, ctx, rank, world, args):
@@ -496,7 +515,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--pretrain", type=int, default=2000)
