@@ -161,6 +161,7 @@ struct Nccl {
     decltype(&ncclGetUniqueId) get_unique_id = nullptr;
     decltype(&ncclCommInitRank) comm_init_rank = nullptr;
     decltype(&ncclAllReduce) all_reduce = nullptr;
+    decltype(&ncclAllGather) all_gather = nullptr;
     decltype(&ncclCommDestroy) comm_destroy = nullptr;
     bool load() {
         if (loaded) return true;
@@ -172,8 +173,9 @@ struct Nccl {
         get_unique_id = reinterpret_cast<decltype(get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
         comm_init_rank = reinterpret_cast<decltype(comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
         all_reduce = reinterpret_cast<decltype(all_reduce)>(dlsym(h, "ncclAllReduce"));
+        all_gather = reinterpret_cast<decltype(all_gather)>(dlsym(h, "ncclAllGather"));
         comm_destroy = reinterpret_cast<decltype(comm_destroy)>(dlsym(h, "ncclCommDestroy"));
-        loaded = get_unique_id && comm_init_rank && all_reduce && comm_destroy;
+        loaded = get_unique_id && comm_init_rank && all_reduce && all_gather && comm_destroy;
         return loaded;
     }
 };
@@ -248,6 +250,22 @@ struct Context {
     // data parallel
     ncclComm_t comm = nullptr;
     uint32_t dp_rank = 0, dp_world = 1;
+    // Peer mode: every rank's model arena mapped here (own base at dp_rank).
+    bool dp_peer = false;
+    unsigned char* peer_model[kMaxDpWorld] = {};
+    float* dp_gsum = nullptr;   // owned range of summed gradients
+    DpSync* dp_sync = nullptr;  // this rank's synchronisation words (model arena)
+    float* mlp_sum = nullptr;   // MLP gradients + loss summed over the ranks (model arena)
+    DpPeers dp_peers() const;
+    uint64_t dp_lo(uint32_t r) const { return (n_grid / 8u) * r / dp_world * 8u; }
+    template <class T>
+    T* peer(uint32_t r, const T* local) const {  // the same buffer in rank r's model arena
+        return reinterpret_cast<T*>(peer_model[r] + (reinterpret_cast<const unsigned char*>(local) - model.base));
+    }
+    NerfStatus open_peers();
+    // Host copy of a buffer of the model arena whose grid part is sharded over
+    // the ranks in peer mode (masters, moments): each range from its owner.
+    cudaError_t read_sharded(void* host, const float* local, uint64_t n) const;
 
     ~Context() { release_all(); }
     void release_graph() {
@@ -272,6 +290,10 @@ struct Context {
         fork_ev = join_ev = nullptr;
         if (side) cudaStreamDestroy(side);
         side = nullptr;
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r)
+            if (peer_model[r] && r != dp_rank) cudaIpcCloseMemHandle(peer_model[r]);
+        for (auto& p : peer_model) p = nullptr;
+        dp_peer = false;
         if (comm && g_nccl.loaded) g_nccl.comm_destroy(comm);
         comm = nullptr;
         if (stream) cudaStreamDestroy(stream);
@@ -353,6 +375,7 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     const uint64_t o_master = model.add(n_params * 4), o_m = model.add(n_params * 4), o_v = model.add(n_params * 4);
     const uint64_t o_p16 = model.add(n_params * 2), o_gg = model.add(n_grid * 2);
     const uint64_t o_mg = model.add(kMlpGradSlots * 4), o_st = model.add(sizeof(DeviceState));
+    const uint64_t o_sync = model.add(sizeof(DpSync)), o_msum = model.add(kMlpGradSlots * 4);
     if (model.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
     master = model.at<float>(o_master);
     m = model.at<float>(o_m);
@@ -361,6 +384,9 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     grid_grad = model.at<__half>(o_gg);
     mlp_grad = model.at<float>(o_mg);
     state = model.at<DeviceState>(o_st);
+    dp_sync = model.at<DpSync>(o_sync);
+    mlp_sum = model.at<float>(o_msum);
+    NB_TRY(cudaMemsetAsync(dp_sync, 0, sizeof(DpSync), stream));
 
     // occupancy arena
     occ.align = model.align;
@@ -493,6 +519,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     const uint64_t o_raw = batch.add(cap * 16u), o_dout = batch.add(cap * 16u), o_dfeat = batch.add(cap * 64u);
     const uint64_t o_part = batch.add(static_cast<uint64_t>(n_partials) * kMlpParams * 4u);
     const uint64_t o_sig = batch.add(std::max<uint32_t>(t.update_count, 1u) * 4ull);
+    const uint64_t own_max = dp_peer ? ((n_grid / 8u + dp_world - 1u) / dp_world + 1u) * 8u : 1u;
+    const uint64_t o_gsum = batch.add(own_max * 4u);
     if (batch.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
     ray_counts = batch.at<uint32_t>(o_rc);
     masks = batch.at<uint32_t>(o_mask);
@@ -510,6 +538,7 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     dfeat = batch.at<void>(o_dfeat);
     partials = batch.at<float>(o_part);
     occ_sigma = batch.at<float>(o_sig);
+    dp_gsum = batch.at<float>(o_gsum);
     NB_TRY(cudaMemsetAsync(batch.base, 0, batch.size, stream));
 
     // Fresh optimiser / occupancy / step state (reference backend-cuda.cu:2205-2215).
@@ -619,6 +648,12 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     op.n_grid = n_grid;
     op.n_params = n_params;
     op.stats_blocks = grad_stats_blocks(n_params);
+    op.mlp_in = mlp_grad;
+    if (dp_peer) {
+        op.dp_peer = 1u;
+        op.dp = dp_peers();
+        op.mlp_in = mlp_sum;
+    }
 
     cudaError_t e;
     int k = 0;
@@ -631,7 +666,17 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = launch_composite(ca, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_field_backward(fa, kFieldTrain, n_partials, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_wgrad_reduce(op, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if (comm) {
+    if (comm && dp_peer) {
+        // Peer mode, no collective library in the step: after a barrier (every
+        // rank's gradients are complete) each rank sums its owned range of all
+        // ranks' hash gradients and all ranks' MLP gradients over NVLink and
+        // publishes its owned range's sum of squares; after a second barrier
+        // (every rank has read this rank's gradients) they are cleared.
+        if ((e = launch_dp_barrier(op.dp, s)) != cudaSuccess || (e = launch_dp_reduce_grads(op, s)) != cudaSuccess ||
+            (e = launch_dp_barrier(op.dp, s)) != cudaSuccess ||
+            (e = cudaMemsetAsync(grid_grad, 0, n_grid * 2u, s)) != cudaSuccess)
+            return e;
+    } else if (comm) {
         if (g_nccl.all_reduce(grid_grad, grid_grad, n_grid, ncclFloat16, ncclSum, comm, s) != ncclSuccess ||
             g_nccl.all_reduce(mlp_grad, mlp_grad, kMlpGradSlots, ncclFloat32, ncclSum, comm, s) != ncclSuccess)
             return cudaErrorUnknown;
@@ -643,10 +688,93 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = cudaEventRecord(fork_ev, s)) != cudaSuccess || (e = cudaStreamWaitEvent(side, fork_ev, 0)) != cudaSuccess ||
         (e = launch_march(sa, side)) != cudaSuccess || (e = cudaEventRecord(join_ev, side)) != cudaSuccess)
         return e;
-    if ((e = launch_adam(op, s)) != cudaSuccess || (e = cudaStreamWaitEvent(s, join_ev, 0)) != cudaSuccess ||
-        (e = mark()) != cudaSuccess)
-        return e;
+    if ((e = launch_adam(op, s)) != cudaSuccess || (e = cudaStreamWaitEvent(s, join_ev, 0)) != cudaSuccess) return e;
+    // Peer mode: every rank wrote its owned fp16 parameters into every rank's
+    // mirror; no rank reads them before all writes are done.
+    if (comm && dp_peer && (e = launch_dp_barrier(op.dp, s)) != cudaSuccess) return e;
+    if ((e = mark()) != cudaSuccess) return e;
     return cudaSuccess;
+}
+
+// Maps every rank's model arena into this process (CUDA IPC; handles
+// exchanged with an NCCL all-gather).  All ranks agree on the result through a
+// min all-reduce, so either all use peer mode or all keep the all-reduce path.
+NerfStatus Context::open_peers() {
+    const char* env = std::getenv("NERF_B200_DP_PEER");
+    bool want = dp_world <= kMaxDpWorld && !(env && env[0] == '0');
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    cudaIpcMemHandle_t mine{};
+    if (want && cudaIpcGetMemHandle(&mine, model.base) != cudaSuccess) {
+        cudaGetLastError();
+        want = false;
+    }
+    unsigned char* dbuf = nullptr;
+    if (cudaMalloc(&dbuf, hb * (dp_world + 1u) + 16u) != cudaSuccess) return NERF_STATUS_FAILURE;
+    std::vector<unsigned char> all(hb * dp_world);
+    float* flag = reinterpret_cast<float*>(dbuf + hb * (dp_world + 1u));
+    bool ok = cudaMemcpy(dbuf + hb * dp_world, &mine, hb, cudaMemcpyHostToDevice) == cudaSuccess &&
+              g_nccl.all_gather(dbuf + hb * dp_world, dbuf, hb, ncclUint8, comm, stream) == ncclSuccess &&
+              cudaStreamSynchronize(stream) == cudaSuccess &&
+              cudaMemcpy(all.data(), dbuf, hb * dp_world, cudaMemcpyDeviceToHost) == cudaSuccess;
+    bool opened = ok && want;
+    if (opened) {
+        for (uint32_t r = 0; r < dp_world; ++r) {
+            if (r == dp_rank) {
+                peer_model[r] = model.base;
+                continue;
+            }
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, all.data() + hb * r, hb);
+            void* p = nullptr;
+            if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+                cudaGetLastError();
+                opened = false;
+                break;
+            }
+            peer_model[r] = static_cast<unsigned char*>(p);
+        }
+    }
+    const float f = opened ? 1.0f : 0.0f;
+    float agreed = 0.0f;
+    ok = ok && cudaMemcpy(flag, &f, 4, cudaMemcpyHostToDevice) == cudaSuccess &&
+         g_nccl.all_reduce(flag, flag, 1, ncclFloat32, ncclMin, comm, stream) == ncclSuccess &&
+         cudaStreamSynchronize(stream) == cudaSuccess && cudaMemcpy(&agreed, flag, 4, cudaMemcpyDeviceToHost) == cudaSuccess;
+    cudaFree(dbuf);
+    dp_peer = ok && agreed > 0.5f;
+    if (!dp_peer) {
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r)
+            if (peer_model[r] && r != dp_rank) cudaIpcCloseMemHandle(peer_model[r]);
+        for (auto& p : peer_model) p = nullptr;
+    }
+    return ok ? NERF_STATUS_OK : NERF_STATUS_FAILURE;
+}
+
+DpPeers Context::dp_peers() const {
+    DpPeers d{};
+    d.world = dp_world;
+    d.rank = dp_rank;
+    d.lo = dp_lo(dp_rank);
+    d.hi = dp_lo(dp_rank + 1u);
+    for (uint32_t r = 0; r < dp_world; ++r) {
+        d.grad[r] = peer(r, grid_grad);
+        d.mlp[r] = peer(r, mlp_grad);
+        d.p16[r] = peer(r, p16);
+        d.sync[r] = peer(r, dp_sync);
+    }
+    d.gsum = dp_gsum;
+    d.mlp_sum = mlp_sum;
+    return d;
+}
+
+cudaError_t Context::read_sharded(void* host, const float* local, uint64_t n) const {
+    if (!dp_peer) return cudaMemcpy(host, local, n * 4u, cudaMemcpyDeviceToHost);
+    float* h = static_cast<float*>(host);
+    for (uint32_t r = 0; r < dp_world; ++r) {
+        const uint64_t lo = dp_lo(r), hi = dp_lo(r + 1u);
+        const cudaError_t e = cudaMemcpy(h + lo, peer(r, local) + lo, (hi - lo) * 4u, cudaMemcpyDefault);
+        if (e != cudaSuccess) return e;
+    }
+    return n > n_grid ? cudaMemcpy(h + n_grid, local + n_grid, (n - n_grid) * 4u, cudaMemcpyDeviceToHost) : cudaSuccess;
 }
 
 NerfStatus Context::capture_graph() {
@@ -974,9 +1102,13 @@ NERF_API NerfStatus nerf_read_train_stats(void* context, NerfTrainStats* out) {
     std::lock_guard<std::mutex> lk(c->mu);
     if (!c->configured) return NERF_STATUS_STATE_ERROR;
     NB_TRY(cudaMemcpyAsync(out, &c->state->stats, sizeof(NerfTrainStats), cudaMemcpyDeviceToHost, c->stream));
+    uint32_t dp_error = 0u;
+    if (c->dp_peer) NB_TRY(cudaMemcpyAsync(&dp_error, &c->dp_sync->error, 4, cudaMemcpyDeviceToHost, c->stream));
     NB_TRY(cudaStreamSynchronize(c->stream));
     c->host_generation = out->completed_steps;
-    return NERF_STATUS_OK;
+    // A data-parallel barrier that timed out (a rank stopped stepping): the
+    // replicas are no longer in step.
+    return dp_error ? NERF_STATUS_CUDA_ERROR : NERF_STATUS_OK;
 }
 
 NERF_API NerfStatus nerf_inference(void* context, const NerfInferenceRequest* req, NerfInferenceInfo* info) {
@@ -1017,7 +1149,7 @@ NERF_API NerfStatus nerf_save_network_weights(void* context, const NerfCheckpoin
     std::lock_guard<std::mutex> lk(c->mu);
     std::vector<float> host(c->n_params);
     NB_TRY(cudaStreamSynchronize(c->stream));
-    NB_TRY(cudaMemcpy(host.data(), c->master, c->n_params * 4, cudaMemcpyDeviceToHost));
+    NB_TRY(c->read_sharded(host.data(), c->master, c->n_params));
     const auto tensors = nb::ckpt::layout(c->n_grid);
     std::string h = "{\"__metadata__\":{\"format\":\"nerf-b200/network-v1\"";
     char buf[512];
@@ -1142,10 +1274,10 @@ NERF_API NerfStatus nerf_b200_read_params(void* context, float* master, uint16_t
     std::lock_guard<std::mutex> lk(c->mu);
     NB_TRY(cudaStreamSynchronize(c->stream));
     const uint64_t n = c->n_params;
-    if (master) NB_TRY(cudaMemcpy(master, c->master, n * 4, cudaMemcpyDeviceToHost));
+    if (master) NB_TRY(c->read_sharded(master, c->master, n));
     if (p16) NB_TRY(cudaMemcpy(p16, c->p16, n * 2, cudaMemcpyDeviceToHost));
-    if (am) NB_TRY(cudaMemcpy(am, c->m, n * 4, cudaMemcpyDeviceToHost));
-    if (av) NB_TRY(cudaMemcpy(av, c->v, n * 4, cudaMemcpyDeviceToHost));
+    if (am) NB_TRY(c->read_sharded(am, c->m, n));
+    if (av) NB_TRY(c->read_sharded(av, c->v, n));
     return NERF_STATUS_OK;
 }
 
@@ -1241,7 +1373,9 @@ NERF_API NerfStatus nerf_b200_dp_init(void* context, uint32_t rank, uint32_t wor
         c->comm = nullptr;
         return NERF_STATUS_FAILURE;
     }
-    c->configured = false;  // the step graph must be recaptured with the all-reduce
+    const NerfStatus ps = c->open_peers();
+    if (ps != NERF_STATUS_OK) return ps;
+    c->configured = false;  // the step graph must be recaptured with the exchange
     return NERF_STATUS_OK;
 }
 
@@ -1395,6 +1529,7 @@ NERF_API NerfStatus nerf_b200_adam(float* master, void* p16, void* grid_grad, co
     o.params16 = p16;
     o.grid_grad = grid_grad;
     o.mlp_grad = const_cast<float*>(mlp_grad);
+    o.mlp_in = mlp_grad;
     o.m = am;
     o.v = av;
     o.n_grid = n_grid;

@@ -129,6 +129,21 @@ struct OccupancyArgs {
 cudaError_t launch_occupancy_update(const OccupancyArgs& a, cudaStream_t s);
 
 // ---- optimiser ----
+// Data-parallel step over peer memory (one process per GPU, the model arenas
+// of all ranks mapped into every rank): each rank owns the grid parameters
+// [lo, hi); it sums every rank's gradients of that range, runs Adam on it and
+// writes the fp16 parameters into every rank's mirror.
+constexpr uint32_t kMaxDpWorld = kMaxDpRanks;
+struct DpPeers {
+    uint32_t world, rank;
+    uint64_t lo, hi;                    // owned grid-parameter range (multiples of 8)
+    const void* grad[kMaxDpWorld];      // every rank's fp16 grid gradients (own included)
+    const float* mlp[kMaxDpWorld];      // every rank's fp32 MLP gradients + loss slot
+    void* p16[kMaxDpWorld];             // every rank's fp16 parameter mirror
+    DpSync* sync[kMaxDpWorld];          // every rank's synchronisation words
+    float* gsum;                        // [hi - lo] summed gradients of the owned range
+    float* mlp_sum;                     // [kMlpGradSlots] summed MLP gradients and loss
+};
 struct OptimArgs {
     TrainConsts tc;
     DeviceState* state;
@@ -144,12 +159,24 @@ struct OptimArgs {
     uint64_t n_params;       // grid + MLP
     uint32_t stats_blocks;
     AdamScalars direct_scalars;  // used when state is null (kernel-level entry point)
+    uint32_t dp_peer;            // 1: gradients summed over the ranks by k_dp_reduce_grads (DpPeers)
+    DpPeers dp;
+    const float* mlp_in;         // MLP gradients + loss read by statistics and Adam (mlp_grad, or dp.mlp_sum)
 };
 cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s);
 uint32_t grad_stats_blocks(uint64_t n_params);
 cudaError_t launch_f32_to_f16(const float* src, void* dst, uint64_t n, cudaStream_t s);
+// Sum of every rank's grid gradients over the owned range into dp.gsum and of
+// every rank's MLP gradients into dp.mlp_sum; the owned range's sum of squares
+// and non-finite flag go to every rank's DpSync::partials.
+cudaError_t launch_dp_reduce_grads(const OptimArgs& a, cudaStream_t s);
+// Barrier of all ranks over their DpSync words: each rank announces a new
+// epoch to every rank and waits (at most five seconds, then DpSync::error) until
+// every rank has announced it.  Writes made before it (by this rank's earlier
+// kernels, to any rank's memory) are visible to every rank after it.
+cudaError_t launch_dp_barrier(const DpPeers& d, cudaStream_t s);
 
 // ---- render ----
 struct RenderArgs {

@@ -51,7 +51,9 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     const uint4* gg = static_cast<const uint4*>(a.grid_grad);
     float sum = 0.0f;
     uint32_t bad = 0u;
-    for (uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n_chunks;
+    // Data-parallel peer mode: the grid part was reduced by k_dp_reduce_grads.
+    const uint64_t q0 = a.dp_peer ? grid_chunks : 0u;
+    for (uint64_t q = q0 + static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n_chunks;
          q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
         float v[8];
         if (q < grid_chunks) {
@@ -64,7 +66,7 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
                 v[2 * k + 1] = f.y;
             }
         } else {
-            const float4* mg = reinterpret_cast<const float4*>(a.mlp_grad + 8u * (q - grid_chunks));
+            const float4* mg = reinterpret_cast<const float4*>(a.mlp_in + 8u * (q - grid_chunks));
             const float4 x = mg[0], y = mg[1];
             v[0] = x.x; v[1] = x.y; v[2] = x.z; v[3] = x.w;
             v[4] = y.x; v[5] = y.y; v[6] = y.z; v[7] = y.w;
@@ -102,9 +104,16 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     __threadfence();
     DeviceState* st = a.state;
     const TrainConsts& tc = a.tc;
-    const float sumsq = atomicAdd(&st->grad_sumsq, 0.0f);
-    const uint32_t nonfinite = atomicOr(&st->nonfinite, 0u);
-    const float loss = *reinterpret_cast<volatile float*>(a.mlp_grad + kMlpGradLoss);
+    float sumsq = atomicAdd(&st->grad_sumsq, 0.0f);
+    uint32_t nonfinite = atomicOr(&st->nonfinite, 0u);
+    if (a.dp_peer) {  // every rank's owned range, in rank order (the same sum on every rank)
+        const volatile DpSync* me = a.dp.sync[a.dp.rank];
+        for (uint32_t r = 0; r < a.dp.world; ++r) {
+            sumsq += me->partials[r][0];
+            nonfinite |= me->partials[r][1] > 0.0f ? 1u : 0u;
+        }
+    }
+    const float loss = *reinterpret_cast<volatile const float*>(a.mlp_in + kMlpGradLoss);
     const float grad_norm = sqrtf(fmaxf(0.0f, sumsq)) / tc.loss_scale;
     const uint32_t has_nonfinite = (nonfinite != 0u || !isfinite(loss) || !isfinite(grad_norm)) ? 1u : 0u;
     const uint32_t frame = st->frame_index;
@@ -147,7 +156,13 @@ struct Chunk {
 };
 
 __device__ __forceinline__ void load_chunk(const OptimArgs& a, uint64_t q, uint64_t grid_chunks, Chunk& c) {
-    if (q < grid_chunks) {
+    if (a.dp_peer && q < grid_chunks) {  // summed gradients of the owned range
+        const float4 x = reinterpret_cast<const float4*>(a.dp.gsum)[q - a.dp.lo / 4u];
+        c.g[0] = x.x;
+        c.g[1] = x.y;
+        c.g[2] = x.z;
+        c.g[3] = x.w;
+    } else if (q < grid_chunks) {
         const uint2 u = static_cast<const uint2*>(a.grid_grad)[q];
         const float2 f0 = unpack_h2(u.x), f1 = unpack_h2(u.y);
         c.g[0] = f0.x;
@@ -155,7 +170,7 @@ __device__ __forceinline__ void load_chunk(const OptimArgs& a, uint64_t q, uint6
         c.g[2] = f1.x;
         c.g[3] = f1.y;
     } else {
-        const float4 x = reinterpret_cast<const float4*>(a.mlp_grad)[q - grid_chunks];
+        const float4 x = reinterpret_cast<const float4*>(a.mlp_in)[q - grid_chunks];
         c.g[0] = x.x;
         c.g[1] = x.y;
         c.g[2] = x.z;
@@ -167,7 +182,7 @@ __device__ __forceinline__ void load_chunk(const OptimArgs& a, uint64_t q, uint6
 }
 
 __device__ __forceinline__ void adam_chunk(const OptimArgs& a, uint64_t q, uint64_t grid_chunks, Chunk& c, const AdamScalars& s) {
-    if (q < grid_chunks) static_cast<uint2*>(a.grid_grad)[q] = make_uint2(0u, 0u);  // cleared for the next step
+    if (q < grid_chunks && !a.dp_peer) static_cast<uint2*>(a.grid_grad)[q] = make_uint2(0u, 0u);  // cleared for the next step
     if (s.skip_update) return;
     float* w = reinterpret_cast<float*>(&c.w);
     float* mm = reinterpret_cast<float*>(&c.m);
@@ -190,31 +205,173 @@ __device__ __forceinline__ void adam_chunk(const OptimArgs& a, uint64_t q, uint6
     __stcs(reinterpret_cast<float4*>(a.master) + q, c.w);
     __stcs(reinterpret_cast<float4*>(a.m) + q, c.m);
     __stcs(reinterpret_cast<float4*>(a.v) + q, c.v);
-    reinterpret_cast<uint2*>(a.params16)[q] = make_uint2(pack_h2(w[0], w[1]), pack_h2(w[2], w[3]));
+    const uint2 h = make_uint2(pack_h2(w[0], w[1]), pack_h2(w[2], w[3]));
+    if (a.dp_peer && q < grid_chunks) {
+        for (uint32_t r = 0; r < a.dp.world; ++r) reinterpret_cast<uint2*>(a.dp.p16[r])[q] = h;  // every rank's mirror
+    } else {
+        reinterpret_cast<uint2*>(a.params16)[q] = h;
+    }
 }
 
 // Grid-stride pass over 4-parameter chunks of the flat vector (hash part
 // first).  The loads of the next chunk are issued before the current one is
 // updated, and the first chunk's loads before the step scalars are read, so
 // each thread keeps two chunks of loads in flight.
+// Chunk k of the pass: the whole flat vector, or (data-parallel peer mode)
+// the owned grid range followed by the MLP part.
+__device__ __forceinline__ uint64_t adam_chunk_index(const OptimArgs& a, uint64_t k, uint64_t grid_chunks) {
+    if (!a.dp_peer) return k;
+    const uint64_t lo = a.dp.lo / 4u, own = (a.dp.hi - a.dp.lo) / 4u;
+    return k < own ? lo + k : grid_chunks + (k - own);
+}
+
 __global__ void __launch_bounds__(256) k_adam(const OptimArgs a, const AdamScalars* __restrict__ sp, const AdamScalars direct) {
-    const uint64_t n_chunks = a.n_params / 4u, grid_chunks = a.n_grid / 4u;
+    const uint64_t grid_chunks = a.n_grid / 4u;
+    const uint64_t n_chunks = a.dp_peer ? (a.dp.hi - a.dp.lo) / 4u + (a.n_params - a.n_grid) / 4u : a.n_params / 4u;
     const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-    uint64_t q = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (q >= n_chunks) return;
+    uint64_t k = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k >= n_chunks) return;
     Chunk cur;
+    uint64_t q = adam_chunk_index(a, k, grid_chunks);
     load_chunk(a, q, grid_chunks, cur);
     const AdamScalars s = sp ? *sp : direct;
     for (;;) {
-        const uint64_t qn = q + stride;
+        const uint64_t kn = k + stride;
         Chunk nxt;
-        const bool more = qn < n_chunks;
+        const bool more = kn < n_chunks;
+        const uint64_t qn = more ? adam_chunk_index(a, kn, grid_chunks) : 0u;
         if (more) load_chunk(a, qn, grid_chunks, nxt);
         adam_chunk(a, q, grid_chunks, cur, s);
         if (!more) break;
         cur = nxt;
+        k = kn;
         q = qn;
     }
+}
+
+// Data-parallel peer mode: every rank's gradients of the owned range, 8 per
+// thread (16-byte loads over NVLink), summed in fp32 in rank order; every
+// rank's MLP gradients and loss, summed in rank order into mlp_sum.  The last
+// block publishes the owned range's sum of squares to every rank.
+__global__ void __launch_bounds__(256) k_dp_reduce_grads(const OptimArgs a) {
+    const uint64_t lo8 = a.dp.lo / 8u, hi8 = a.dp.hi / 8u;
+    const uint64_t tid = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    for (uint64_t i = tid; i < kMlpGradSlots / 4u; i += stride) {
+        float4 x[kMaxDpWorld];
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r)  // all loads in flight before the sum
+            x[r] = r < a.dp.world ? __ldcv(reinterpret_cast<const float4*>(a.dp.mlp[r]) + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        float4 s4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r) {
+            if (r >= a.dp.world) break;
+            s4.x += x[r].x;
+            s4.y += x[r].y;
+            s4.z += x[r].z;
+            s4.w += x[r].w;
+        }
+        reinterpret_cast<float4*>(a.dp.mlp_sum)[i] = s4;
+    }
+    float sum = 0.0f;
+    uint32_t bad = 0u;
+    for (uint64_t q = lo8 + tid; q < hi8; q += stride) {
+        uint4 u[kMaxDpWorld];
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r)  // all loads in flight before the sum
+            u[r] = r < a.dp.world ? __ldcv(static_cast<const uint4*>(a.dp.grad[r]) + q) : make_uint4(0u, 0u, 0u, 0u);
+        float v[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r) {
+            if (r >= a.dp.world) break;
+            const uint32_t w[4] = {u[r].x, u[r].y, u[r].z, u[r].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = unpack_h2(w[k]);
+                v[2 * k] += f.x;
+                v[2 * k + 1] += f.y;
+            }
+        }
+        float4* dst = reinterpret_cast<float4*>(a.dp.gsum + (q - lo8) * 8u);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            if (!isfinite(v[k])) bad = 1u;
+            else sum = fmaf(v[k], v[k], sum);
+        }
+    }
+    __shared__ float ps[8];
+    __shared__ uint32_t pb[8];
+    __shared__ bool last;
+    const float ws = warp_sum(sum);
+    const uint32_t wb = __any_sync(0xffffffffu, bad != 0u) ? 1u : 0u;
+    if ((threadIdx.x & 31u) == 0u) {
+        ps[threadIdx.x >> 5] = ws;
+        pb[threadIdx.x >> 5] = wb;
+    }
+    __syncthreads();
+    DpSync* me = a.dp.sync[a.dp.rank];
+    if (threadIdx.x == 0u) {
+        float bs = 0.0f;
+        uint32_t bb = 0u;
+        for (uint32_t w = 0; w < blockDim.x / 32u; ++w) {
+            bs += ps[w];
+            bb |= pb[w];
+        }
+        if (bs != 0.0f) atomicAdd(&me->sum, bs);
+        if (bb) atomicOr(&me->bad, 1u);
+        __threadfence();
+        last = atomicAdd(&me->done, 1u) == gridDim.x - 1u;
+    }
+    __syncthreads();
+    if (!last || threadIdx.x >= a.dp.world) return;
+    __threadfence();
+    const float total = atomicAdd(&me->sum, 0.0f);
+    const float flag = atomicOr(&me->bad, 0u) ? 1.0f : 0.0f;
+    DpSync* dst = a.dp.sync[threadIdx.x];  // every rank's slot for this rank
+    dst->partials[a.dp.rank][0] = total;
+    dst->partials[a.dp.rank][1] = flag;
+    __syncwarp(0xffffffffu >> (32u - a.dp.world));
+    if (threadIdx.x == 0u) {
+        me->sum = 0.0f;
+        me->bad = 0u;
+        me->done = 0u;
+    }
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__global__ void __launch_bounds__(32) k_dp_barrier(const DpPeers d) {
+    __shared__ uint32_t epoch;
+    DpSync* me = d.sync[d.rank];
+    if (threadIdx.x == 0u) {
+        epoch = me->epoch + 1u;
+        me->epoch = epoch;
+    }
+    __syncthreads();
+    const uint32_t t = threadIdx.x;
+    if (t < d.world) {
+        __threadfence_system();
+        asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(&d.sync[t]->flags[d.rank]), "r"(epoch) : "memory");
+        const uint64_t t0 = global_ns();
+        for (;;) {
+            uint32_t seen;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(seen) : "l"(&me->flags[t]) : "memory");
+            if (static_cast<int32_t>(seen - epoch) >= 0) break;
+            if (global_ns() - t0 > 5000000000ull) {  // five seconds: give up, report, go on
+                atomicExch(&me->error, 1u);
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    __syncthreads();
+    __threadfence_system();
 }
 
 __global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__ dst, uint64_t n) {
@@ -250,8 +407,18 @@ cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {
     k_grad_stats<<<a.stats_blocks, 256, 0, s>>>(a);
     return cudaGetLastError();
 }
+cudaError_t launch_dp_reduce_grads(const OptimArgs& a, cudaStream_t s) {
+    if (!a.dp_peer || a.dp.world == 0u || a.dp.world > kMaxDpWorld) return cudaErrorInvalidValue;
+    k_dp_reduce_grads<<<4u * sm_count(), 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+cudaError_t launch_dp_barrier(const DpPeers& d, cudaStream_t s) {
+    if (d.world == 0u || d.world > kMaxDpWorld || d.rank >= d.world) return cudaErrorInvalidValue;
+    k_dp_barrier<<<1, 32, 0, s>>>(d);
+    return cudaGetLastError();
+}
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s) {
-    const uint64_t chunks = a.n_params / 4u;
+    const uint64_t chunks = a.dp_peer ? (a.dp.hi - a.dp.lo) / 4u + (a.n_params - a.n_grid) / 4u : a.n_params / 4u;
     uint64_t blocks = (chunks + 255u) / 256u;
     const uint64_t cap = 4ull * sm_count();  // 4 resident blocks per SM, grid-stride beyond
     if (blocks > cap) blocks = cap;

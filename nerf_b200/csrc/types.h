@@ -84,6 +84,21 @@ struct DeviceState {
     unsigned long long total_rays;
 };
 
+// Data-parallel peer mode: synchronisation words of one rank, in its model
+// arena (mapped by every rank).  Zeroed at creation, never reset afterwards:
+// barrier epochs only grow.
+constexpr uint32_t kMaxDpRanks = 8;
+struct DpSync {
+    uint32_t flags[kMaxDpRanks];        // flags[q]: last barrier epoch rank q announced to this rank
+    float partials[kMaxDpRanks][2];     // partials[q]: rank q's owned-range sum of squares, non-finite flag
+    uint32_t epoch;                     // this rank's last barrier epoch
+    uint32_t done;                      // last-block counter of the gradient reduction
+    uint32_t error;                     // a barrier wait ran out of time
+    uint32_t bad;                       // non-finite flag of the gradient reduction in progress
+    float sum;                          // sum of squares of the gradient reduction in progress
+    uint32_t pad[3];
+};
+
 // Per-step constants of the training graph, passed by value to kernels.
 struct TrainConsts {
     // scene

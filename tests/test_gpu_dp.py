@@ -1,12 +1,16 @@
-"""Data-parallel GPU training over NCCL (needs two GPUs; skipped otherwise).
+"""Data-parallel GPU training (needs two GPUs; skipped otherwise).
 
-Two processes, one per GPU, train through nerf_b200_dp_init + nerf_train_step.
-Both replicas must be bitwise identical after every step (same summed
-gradients, same Adam); each rank's sample stream must equal the oracle's for
-that rank bit for bit; the first Adam moment (the clipped, summed gradient)
-must match the two-rank oracle emulation within the tolerances of the
-single-GPU test.
+Two processes, one per GPU, train through nerf_b200_dp_init + nerf_train_step,
+in both exchange modes: peer mode (each rank sums its owned range of every
+rank's hash gradients over NVLink, runs Adam on it and writes the fp16
+parameters into every rank's mirror) and the NCCL all-reduce path
+(NERF_B200_DP_PEER=0).  Both replicas must be bitwise identical after every
+step; each rank's sample stream must equal the oracle's for that rank bit for
+bit; the first Adam moment (the clipped, summed gradient) must match the
+two-rank oracle emulation within the tolerances of the single-GPU test.
 """
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -18,12 +22,22 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_gpu_training_matches_oracle():
-    res = _run(dp_worker.gpu_rank, 2, 1)
+@pytest.mark.parametrize("peer", ["1", "0"])
+@pytest.mark.parametrize("steps", [1, 3])
+def test_two_gpu_training_matches_oracle(peer, steps):
+    old = os.environ.get("NERF_B200_DP_PEER")
+    os.environ["NERF_B200_DP_PEER"] = peer
+    try:
+        res = _run(dp_worker.gpu_rank, 2, steps)
+    finally:
+        if old is None:
+            del os.environ["NERF_B200_DP_PEER"]
+        else:
+            os.environ["NERF_B200_DP_PEER"] = old
     (g0, m0, c0, l0), (g1, m1, c1, l1) = res[0], res[1]
     assert np.array_equal(g0, g1) and np.array_equal(m0, m1), "replicas diverged"
     assert l0 == l1
-    _, batches, params = dp_worker.serial_emulation(2, 1)
+    _, batches, params = dp_worker.serial_emulation(2, steps)
     assert np.array_equal(batches[0]["counts"], c0)
     assert np.array_equal(batches[1]["counts"], c1)
     om = params[0][2]
