@@ -52,13 +52,6 @@ WORKLOAD = ("config2 bounded training: 12 spheres/boxes, 100 views 800x800, hash
             "2^18 target samples/step/GPU, <=1024 steps/ray, 128^3 occupancy every 16 steps, random bg")
 
 
-# Kernel launches of one training step: occupancy query and update, the
-# sampler's bitfield / scan / write kernels, field forward, composite, field
-# backward (MLP kernel + hash scatter kernel), weight-gradient reduce,
-# statistics, Adam and the next step's march.
-KERNELS_PER_STEP = 13
-
-
 def options(nb, **kw):
     return nb.default_options(log2_hashmap_size=19, max_resolution=2048, background=1, stop_transmittance=1e-4,
                               target_samples_per_step=TARGET_SAMPLES, max_samples_per_step=2 * TARGET_SAMPLES, **kw)
@@ -205,6 +198,7 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     c1 = ctx.counters()
+    kernels_per_step = int(c1.kernels_per_step)  # this library's launches per step, as the library counts them
     samples = c1.total_samples - c0.total_samples
     rays = c1.total_rays - c0.total_rays
     t = torch.tensor([ms, float(samples), float(rays)], dtype=torch.float64, device="cuda")
@@ -241,6 +235,7 @@ def run_ours(args):
             k["corner_updates_g_per_s"] = mean_samples * 128 / (k["ms"] / 1e3) / 1e9
             k["l2_red_frac"] = k["corner_updates_g_per_s"] / l2["red_f16x2_gops"]
 
+    psnr = psnr_heldout(nb, ctx, args) if rank == 0 else None
     render = None
     if not args.skip_render:
         render = run_render(nb, ctx, rank, world, args)
@@ -269,11 +264,12 @@ def run_ours(args):
                              "reads a 256 MB image set; the 24 MB hash table is meant to stay L2-resident",
                        "final_loss": stats.loss, "dataset_gen_s": gen_s},
             "e2e": e2e,
-            "gpu_launches": KERNELS_PER_STEP * args.steps,
+            "gpu_launches": kernels_per_step * args.steps,
             "roofline": roofline(dom, hbm, src),
             "l2": l2,
             "kernels": kernels,
             "render": render,
+            "psnr": psnr,
             "cpu_baseline": cpu,
             "clocks": clk,
         }
@@ -369,6 +365,29 @@ def roofline(dom, hbm, src):
             "note": "achieved = algorithmic bytes per launch / mean CUDA-event launch time (kernel-by-kernel step, "
                     "same kernels as the graph); traffic = ncu DRAM bytes per launch; the field kernels are "
                     "L2-bound, see the l2 object and the kernels' l2 fractions"}
+
+
+def psnr_heldout(nb, ctx, args):
+    """PSNR of the trained model on held-out views of the config-2 scene (cameras after the 100 training views,
+    ground truth composited on white, the render's background)."""
+    n = args.psnr_views
+    if n <= 0:
+        return None
+    held = nb.make_scene(**{**CFG2, "n_views": n, "view_offset": CFG2["n_views"], "orbit_views": CFG2["n_views"] + n})
+    W, H = CFG2["width"], CFG2["height"]
+    errs = []
+    img = np.zeros((H, W, 4), np.uint8)
+    for v in range(n):
+        ctx.render(held.cameras[v], W, H, held.intrinsics, max_steps=MAX_STEPS_PER_RAY, stop=1e-4, dst=img)
+        gt = held.images[v].astype(np.float64) / 255.0
+        ref = gt[..., :3] * gt[..., 3:4] + (1.0 - gt[..., 3:4])
+        out = img[..., :3].astype(np.float64) / 255.0
+        errs.append(float(np.mean((out - ref) ** 2)))
+    psnr = [10.0 * np.log10(1.0 / max(e, 1e-12)) for e in errs]
+    return {"value": float(np.mean(psnr)), "unit": "dB", "views": n, "resolution": f"{W}x{H}",
+            "train_steps": args.pretrain + 2 * args.warmup + args.steps,
+            "note": "mean over held-out views (the 20 cameras after the training views) of PSNR against the exact "
+                    "render composited on white; rendered with the training occupancy grid, T < 1e-4 termination"}
 
 
 def run_render(nb, ctx, rank, world, args):
@@ -521,6 +540,7 @@ def main():
     ap.add_argument("--pretrain", type=int, default=2000)
     ap.add_argument("--profile-steps", type=int, default=20)
     ap.add_argument("--render-views", type=int, default=20)
+    ap.add_argument("--psnr-views", type=int, default=20)
     ap.add_argument("--e2e-steps", type=int, default=1000)
     ap.add_argument("--views", type=int, default=None)
     ap.add_argument("--skip-render", action="store_true")

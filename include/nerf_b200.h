@@ -58,6 +58,8 @@ typedef struct NerfB200Counters {
     uint32_t next_rays;            /* rays the next step will march                    */
     uint64_t total_samples;        /* since configure                                  */
     uint64_t total_rays;
+    uint32_t kernels_per_step;     /* this library's kernel launches in one training step */
+    uint32_t dp_peer;              /* 1: data-parallel exchange over peer memory          */
 } NerfB200Counters;
 NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out);
 
@@ -68,8 +70,8 @@ NERF_API NerfStatus nerf_b200_context_stream(void* context, void** stream);
  * graph, with CUDA events between launches.  Segments: occupancy query,
  * occupancy update, sampler (bitfield tests, compaction scan, sample
  * writes), field forward, composite, field backward, weight-gradient
- * reduce, gradient all-reduce (0 on one GPU), gradient statistics, Adam
- * (with the next step's ray march running beside it on a second stream). */
+ * reduce (folded into the statistics on one GPU), gradient exchange (0 on
+ * one GPU), gradient statistics, Adam (with the next step's ray march). */
 #define NERF_B200_STEP_KERNELS 10
 typedef struct NerfB200StepProfile {
     float milliseconds[NERF_B200_STEP_KERNELS];

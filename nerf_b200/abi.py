@@ -151,6 +151,8 @@ class NerfB200Counters(C.Structure):
         ("next_rays", C.c_uint32),
         ("total_samples", C.c_uint64),
         ("total_rays", C.c_uint64),
+        ("kernels_per_step", C.c_uint32),
+        ("dp_peer", C.c_uint32),
     ]
 
 

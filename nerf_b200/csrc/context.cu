@@ -189,8 +189,6 @@ struct Context {
     std::mutex mu;
     int device = 0;
     cudaStream_t stream = nullptr;
-    cudaStream_t side = nullptr;  // the next step's march, beside Adam
-    cudaEvent_t fork_ev = nullptr, join_ev = nullptr;
     NerfB200Options opt{};
     GridLayout grid{};
     LevelTable lt{};
@@ -285,11 +283,6 @@ struct Context {
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         ev0 = ev1 = nullptr;
-        if (fork_ev) cudaEventDestroy(fork_ev);
-        if (join_ev) cudaEventDestroy(join_ev);
-        fork_ev = join_ev = nullptr;
-        if (side) cudaStreamDestroy(side);
-        side = nullptr;
         for (uint32_t r = 0; r < kMaxDpWorld; ++r)
             if (peer_model[r] && r != dp_rank) cudaIpcCloseMemHandle(peer_model[r]);
         for (auto& p : peer_model) p = nullptr;
@@ -365,10 +358,6 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     if (ensure_attributes() != cudaSuccess) return NERF_STATUS_FAILURE;
     if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     if (cudaEventCreate(&ev0) != cudaSuccess || cudaEventCreate(&ev1) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
-    if (cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
-    if (cudaEventCreateWithFlags(&fork_ev, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&join_ev, cudaEventDisableTiming) != cudaSuccess)
-        return NERF_STATUS_CUDA_ERROR;
 
     // model arena
     model.align = std::max<uint64_t>(alignment, 256u);
@@ -665,7 +654,10 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = launch_field_forward(fa, kFieldTrain, fwd_blocks, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_composite(ca, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_field_backward(fa, kFieldTrain, n_partials, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if ((e = launch_wgrad_reduce(op, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    // One GPU: the statistics kernel also reduces the weight-gradient partials.
+    op.fuse_wgrad = comm ? 0u : 1u;
+    if (!op.fuse_wgrad && (e = launch_wgrad_reduce(op, s)) != cudaSuccess) return e;
+    if ((e = mark()) != cudaSuccess) return e;
     if (comm && dp_peer) {
         // Peer mode, no collective library in the step: after a barrier (every
         // rank's gradients are complete) each rank sums its owned range of all
@@ -684,11 +676,9 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = mark()) != cudaSuccess) return e;
     if ((e = launch_grad_stats(op, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     // The statistics kernel advanced the frame and set the next ray count:
-    // the next step's march runs on the side stream beside Adam.
-    if ((e = cudaEventRecord(fork_ev, s)) != cudaSuccess || (e = cudaStreamWaitEvent(side, fork_ev, 0)) != cudaSuccess ||
-        (e = launch_march(sa, side)) != cudaSuccess || (e = cudaEventRecord(join_ev, side)) != cudaSuccess)
-        return e;
-    if ((e = launch_adam(op, s)) != cudaSuccess || (e = cudaStreamWaitEvent(s, join_ev, 0)) != cudaSuccess) return e;
+    // the next step's march.  (Run beside Adam on a second stream it gained
+    // nothing: the concurrent blocks slowed Adam down by the march's time.)
+    if ((e = launch_march(sa, s)) != cudaSuccess || (e = launch_adam(op, s)) != cudaSuccess) return e;
     // Peer mode: every rank wrote its owned fp16 parameters into every rank's
     // mirror; no rank reads them before all writes are done.
     if (comm && dp_peer && (e = launch_dp_barrier(op.dp, s)) != cudaSuccess) return e;
@@ -1246,6 +1236,11 @@ NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out
     out->next_rays = st.n_rays;
     out->total_samples = st.total_samples;
     out->total_rays = st.total_rays;
+    // occupancy query + update, sampler (3), forward, composite, backward MLP +
+    // scatter, statistics, march, Adam; data-parallel: + weight-gradient
+    // reduce, and in peer mode 3 barriers + the gradient reduction.
+    out->kernels_per_step = 12u + (c->comm ? 1u : 0u) + (c->dp_peer ? 4u : 0u);
+    out->dp_peer = c->dp_peer ? 1u : 0u;
     return NERF_STATUS_OK;
 }
 

@@ -89,7 +89,7 @@ struct SamplerArgs {
 constexpr uint32_t kSamplerBlock = 256;
 // Step recurrence of every ray of the step whose frame is in the state.  A
 // step's march only depends on the frame and the ray count, so the training
-// step launches the next step's march beside its Adam update.
+// step ends with the next step's march.
 cudaError_t launch_march(const SamplerArgs& a, cudaStream_t s);
 // Bitfield tests, compaction scan and sample writes (after launch_march).
 cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s);
@@ -162,6 +162,7 @@ struct OptimArgs {
     uint32_t dp_peer;            // 1: gradients summed over the ranks by k_dp_reduce_grads (DpPeers)
     DpPeers dp;
     const float* mlp_in;         // MLP gradients + loss read by statistics and Adam (mlp_grad, or dp.mlp_sum)
+    uint32_t fuse_wgrad;         // statistics kernel also reduces the weight-gradient partials (single GPU)
 };
 cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);

@@ -1,7 +1,8 @@
 // optimizer.cu -- end of a training step.
 //
 //   k_wgrad_reduce  sums the per-CTA MLP weight-gradient partials of the
-//                   backward kernel (deterministic order).
+//                   backward kernel (deterministic order); on one GPU the
+//                   statistics kernel does this in its first blocks.
 //   k_grad_stats    sum of squares and non-finite flag over all gradients
 //                   (fp16 hash-table part, fp32 MLP part); the last block to
 //                   finish derives the step statistics, the update guard,
@@ -45,16 +46,39 @@ __device__ __forceinline__ void adam_scalars(const TrainConsts& tc, float grad_n
     o.skip_update = skip ? 1u : 0u;
 }
 
+constexpr uint32_t kWgradBlocks = (kMlpParams + 255u) / 256u;
+
 __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
-    const uint64_t n_chunks = a.n_params / 8u;
+    uint64_t n_chunks = a.n_params / 8u;
     const uint64_t grid_chunks = a.n_grid / 8u;
     const uint4* gg = static_cast<const uint4*>(a.grid_grad);
     float sum = 0.0f;
     uint32_t bad = 0u;
     // Data-parallel peer mode: the grid part was reduced by k_dp_reduce_grads.
-    const uint64_t q0 = a.dp_peer ? grid_chunks : 0u;
-    for (uint64_t q = q0 + static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; q < n_chunks;
-         q += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    uint64_t q0 = a.dp_peer ? grid_chunks : 0u;
+    uint64_t first = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+    if (a.fuse_wgrad) {
+        // The first blocks sum the backward's per-CTA weight-gradient partials
+        // (fixed order) and take the MLP part of the statistics; the others
+        // take the hash-table part.
+        if (blockIdx.x < kWgradBlocks) {
+            const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+            if (i < kMlpParams) {
+                float g = 0.0f;
+                for (uint32_t c = 0; c < a.n_partials; ++c) g += a.partials[static_cast<unsigned long long>(c) * kMlpParams + i];
+                a.mlp_grad[i] = g;
+                if (!isfinite(g)) bad = 1u;
+                else sum = g * g;
+            }
+            n_chunks = 0u;
+        } else {
+            n_chunks = grid_chunks;
+            first = static_cast<uint64_t>(blockIdx.x - kWgradBlocks) * blockDim.x + threadIdx.x;
+            stride = static_cast<uint64_t>(gridDim.x - kWgradBlocks) * blockDim.x;
+        }
+    }
+    for (uint64_t q = q0 + first; q < n_chunks; q += stride) {
         float v[8];
         if (q < grid_chunks) {
             const uint4 u = gg[q];
@@ -404,7 +428,8 @@ cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {
-    k_grad_stats<<<a.stats_blocks, 256, 0, s>>>(a);
+    if (a.fuse_wgrad && (a.dp_peer || a.n_partials == 0u)) return cudaErrorInvalidValue;
+    k_grad_stats<<<a.stats_blocks + (a.fuse_wgrad ? kWgradBlocks : 0u), 256, 0, s>>>(a);
     return cudaGetLastError();
 }
 cudaError_t launch_dp_reduce_grads(const OptimArgs& a, cudaStream_t s) {

@@ -192,6 +192,35 @@ def test_render_matches_oracle(cuda):
     ctx.close()
 
 
+def _psnr(img_rgba8, gt_rgba8):
+    gt = gt_rgba8.astype(np.float64) / 255.0
+    ref = gt[..., :3] * gt[..., 3:4] + (1.0 - gt[..., 3:4])
+    mse = np.mean((img_rgba8[..., :3].astype(np.float64) / 255.0 - ref) ** 2)
+    return 10.0 * np.log10(1.0 / mse)
+
+
+def test_heldout_psnr_matches_oracle(cuda):
+    """Train the GPU context and the oracle independently from the same
+    initialisation for 60 steps, render held-out views with each, and compare
+    PSNR against the exact renders: within 0.1 dB."""
+    ds, ctx, oc, _ = make_pair(warmup=4, interval=4, n_views=8, size=48)
+    for _ in range(60):
+        ctx.train_step()
+        oc.step()
+    held = nerf_b200.make_scene(kind=0, seed=0, n_views=4, width=48, height=48, fov=0.69, radius=3.0, view_offset=8)
+    g_psnr, o_psnr = [], []
+    out = np.zeros((48, 48, 4), np.uint8)
+    for v in range(4):
+        ctx.render(held.cameras[v], 48, 48, held.intrinsics, max_steps=STEPS, stop=1e-4, dst=out)
+        rgba, _ = oc.render(held.cameras[v], 48, 48, held.intrinsics, STEPS, 1e-4)
+        g_psnr.append(_psnr(out, held.images[v]))
+        o_psnr.append(_psnr(rgba.view(np.uint8).reshape(48, 48, 4), held.images[v]))
+    g, o = float(np.mean(g_psnr)), float(np.mean(o_psnr))
+    assert g > 12.0, g  # it learned something
+    assert abs(g - o) < 0.1, (g, o)
+    ctx.close()
+
+
 def test_inference_abi(cuda):
     ds, ctx, oc, _ = make_pair(warmup=2, interval=1)
     for _ in range(3):
