@@ -338,11 +338,12 @@ def l2_peaks(lib, stream):
     words = 1 << 23
     rb = torch.zeros(words, dtype=torch.int32, device="cuda")
     ops = C.c_uint64()
-    for vec, key in ((0, "red_f16x2_gops"), (1, "red_v2_f16x2_gops")):
+    for vec, key in ((0, "red_f16x2_gops"), (1, "red_v2_f16x2_gops"), (2, "red_v4_f16x2_gops")):
         t = timed(lambda: lib.nerf_b200_probe_l2_red(rb.data_ptr(), words, 64, vec, C.byref(ops), h))
         res[key] = ops.value / t / 1e9
     res["note"] = ("probes: 64 MB L2-resident buffer, 16 sweeps of 16-byte loads; f16x2 reductions at hashed word "
-                   "addresses of a 32 MB buffer (v2: 8-byte form), 64 per thread over 8 blocks x 256 threads per SM")
+                   "addresses of a 32 MB buffer (v2 / v4: 8- / 16-byte forms), 64 per thread over 8 blocks x 256 "
+                   "threads per SM")
     return res
 
 

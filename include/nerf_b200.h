@@ -252,11 +252,12 @@ NERF_API NerfStatus nerf_b200_occupancy_update(float* density, uint32_t* bitfiel
  * `stream`; the caller times them with events.
  * read: `passes` sweeps of 16-byte loads over `bytes` of `buf` (16-byte
  *       aligned; `sink` >= 1024 words, written only to keep loads live).
- * red:  reps f16x2 reductions per thread (8-byte .v2 form when vec2 != 0)
- *       at hashed word indices of `buf` (`words` a power of two); *ops
- *       receives the number of reduction instructions issued. */
+ * red:  reps f16x2 reductions per thread (vec 0: 4-byte form, 1: 8-byte
+ *       .v2, 2: 16-byte .v4) at hashed word indices of `buf` (16-byte
+ *       aligned, `words` a power of two >= 4); *ops receives the number of
+ *       reduction instructions issued. */
 NERF_API NerfStatus nerf_b200_probe_l2_read(const void* buf, uint64_t bytes, uint32_t passes, uint32_t* sink, void* stream);
-NERF_API NerfStatus nerf_b200_probe_l2_red(void* buf, uint32_t words, uint32_t reps, uint32_t vec2, uint64_t* ops,
+NERF_API NerfStatus nerf_b200_probe_l2_red(void* buf, uint32_t words, uint32_t reps, uint32_t vec, uint64_t* ops,
                                            void* stream);
 
 #ifdef __cplusplus

@@ -83,8 +83,8 @@ NB_DEV void level_corners(const float p[3], const LevelParams lp, uint32_t hash_
 // Corners c and c|1 differ only in x.  When their entries form an aligned
 // pair (indices differing in bit 0 only: always on hashed levels for even x,
 // on dense levels for an even first index) both are fetched with one 8-byte
-// load and reduced with one 8-byte f16x2 vector reduction.  Level offsets are
-// multiples of 8 entries, so absolute and level-relative parity agree.
+// load.  Level offsets are multiples of 8 entries, so absolute and
+// level-relative alignment agree.
 NB_DEV void gather_pair(const uint32_t* __restrict__ P, uint32_t ea, uint32_t eb, uint32_t& va, uint32_t& vb) {
     if ((ea ^ eb) == 1u) {
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(P + (ea & ~1u)));
@@ -95,10 +95,19 @@ NB_DEV void gather_pair(const uint32_t* __restrict__ P, uint32_t ea, uint32_t eb
         vb = __ldg(P + eb);
     }
 }
+// Reduction of corners c and c|1: when both entries lie in one aligned
+// 4-entry block (x and x+1 differ only in their two low bits -- 3 cases in
+// 4, on dense and hashed levels alike) one 16-byte .v4 reduction carries both,
+// adding zero to the block's other two entries.  L2 reductions cost per
+// operation, not per byte, so this saves one operation.
 NB_DEV void red_pair(uint32_t* G, uint32_t ea, uint32_t eb, uint32_t va, uint32_t vb) {
-    if ((ea ^ eb) == 1u) {
-        const uint32_t lo = (ea & 1u) ? vb : va, hi = (ea & 1u) ? va : vb;
-        asm volatile("red.global.add.noftz.v2.f16x2 [%0], {%1, %2};\n" ::"l"(G + (ea & ~1u)), "r"(lo), "r"(hi) : "memory");
+    if ((ea ^ eb) < 4u) {
+        uint32_t w[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+        for (uint32_t k = 0; k < 4u; ++k) w[k] = k == (ea & 3u) ? va : (k == (eb & 3u) ? vb : 0u);
+        asm volatile("red.global.add.noftz.v4.f16x2 [%0], {%1, %2, %3, %4};\n" ::"l"(G + (ea & ~3u)), "r"(w[0]), "r"(w[1]),
+                     "r"(w[2]), "r"(w[3])
+                     : "memory");
     } else {
         red_add_f16x2(G + ea, va);
         red_add_f16x2(G + eb, vb);

@@ -4,8 +4,9 @@
 // f16x2 reductions in the backward), for which no driver-measured peak
 // exists.  These two probes measure it on the running GPU:
 //   read  every thread streams 16-byte loads over an L2-resident buffer;
-//   red   every thread issues red.global.add.noftz.f16x2 (or .v2) at hashed
-//         addresses of a buffer the size of a hash table.
+//   red   every thread issues red.global.add.noftz.f16x2 (or the 8-byte .v2
+//         or 16-byte .v4 form) at hashed addresses of a buffer the size of a
+//         hash table.
 #include "common.cuh"
 
 #include "nerf_b200.h"
@@ -31,7 +32,11 @@ __global__ void __launch_bounds__(256) k_probe_red(uint32_t* buf, uint32_t mask,
     const uint32_t v = pack_h2(1.0f / 1024.0f, -1.0f / 1024.0f);
     for (uint32_t i = 0; i < reps; ++i) {
         const uint32_t e = hash_u32(tid * 0x9E3779B9u + i) & mask;
-        if (vec) {
+        if (vec == 2u) {
+            asm volatile("red.global.add.noftz.v4.f16x2 [%0], {%1, %2, %3, %4};\n" ::"l"(buf + (e & ~3u)), "r"(v), "r"(v),
+                         "r"(v), "r"(v)
+                         : "memory");
+        } else if (vec == 1u) {
             asm volatile("red.global.add.noftz.v2.f16x2 [%0], {%1, %2};\n" ::"l"(buf + (e & ~1u)), "r"(v), "r"(v) : "memory");
         } else {
             red_add_f16x2(buf + e, v);
@@ -57,13 +62,13 @@ NERF_API NerfStatus nerf_b200_probe_l2_read(const void* buf, uint64_t bytes, uin
     return cudaGetLastError() == cudaSuccess ? NERF_STATUS_OK : NERF_STATUS_CUDA_ERROR;
 }
 
-NERF_API NerfStatus nerf_b200_probe_l2_red(void* buf, uint32_t words, uint32_t reps, uint32_t vec2, uint64_t* ops,
+NERF_API NerfStatus nerf_b200_probe_l2_red(void* buf, uint32_t words, uint32_t reps, uint32_t vec, uint64_t* ops,
                                            void* stream) {
-    if (!buf || words < 2u || (words & (words - 1u)) || (reinterpret_cast<uintptr_t>(buf) & 7u))
+    if (!buf || words < 4u || (words & (words - 1u)) || (reinterpret_cast<uintptr_t>(buf) & 15u) || vec > 2u)
         return NERF_STATUS_INVALID_USAGE;
     const uint32_t blocks = nb::probe_blocks();
     nb::k_probe_red<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t*>(buf), words - 1u, reps,
-                                                                           vec2 ? 1u : 0u);
+                                                                           vec);
     if (ops) *ops = static_cast<uint64_t>(blocks) * 256u * reps;
     return cudaGetLastError() == cudaSuccess ? NERF_STATUS_OK : NERF_STATUS_CUDA_ERROR;
 }
