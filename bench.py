@@ -23,7 +23,9 @@ from event-timed kernel-by-kernel steps, per-kernel times, render MRays/s
 
 --impl reference times the reference algorithm's CPU implementation (the
 oracle port; the reference backend has no CPU path) on the host cores, rank 0
-only.
+only; its line also carries "reference_cuda": the reference's own CUDA
+backend (built from its sources for sm_100a) timed through its nerf.h on
+this GPU (training samples/s, held-out PSNR, render MRays/s).
 """
 from __future__ import annotations
 
@@ -511,6 +513,146 @@ def cpu_baseline(nb, ds, args, steps=None, threads=None, seconds=20.0):
                       f"{dt:.1f} s, warm-up phase of a fresh job)"}
 
 
+# ------------------------------------------------------------ microbench
+def run_micro(args):
+    """the kernel-level entry points on seeded synthetic inputs, each point against its roofline.
+
+    encode fwd / bwd (nerf_b200_grid_forward / _backward): n points U[0,1]^3, L16 F2 fp16, N_max 2048,
+      T = 2^14..2^24; bwd upstream gradients N(0,1).  Algorithmic bytes per point: fwd 12 in + 128 x 4 gathers +
+      64 out = 588; bwd 12 + 64 in + 128 x 8 read-modify-write = 1100.  Tables that fit L2 are compared with the
+      live L2 probes (fwd: 16-byte L2 read GB/s; bwd: corner reductions / s against the f16x2 reduction rate),
+      larger tables with the measured HBM copy peak.
+    MLP fwd / bwd (nerf_b200_mlp_forward / _backward, the fused field's MLPs on given features): rows of 32 fp16
+      features N(0,1) and unit directions; 20,480 FLOP per row forward, 61,440 backward (forward recompute,
+      input-gradient and weight-gradient products), against the measured dense bf16 peak.
+    composite fwd+bwd (nerf_b200_composite, one fused kernel): 2^16 rays x S samples, sigma ~ Exp(1) (raw =
+      log sigma), rgb U[0,1] (raw = logit), dt = 1/S, no early termination; 88 bytes per sample for this two-pass
+      layout (raw 16 + pos_dt 16 read in each pass, transmittance 8, d raw 16 written), against HBM.
+    Each point: 2 untimed launches, then the mean of `reps` launches between CUDA events on one stream.
+    """
+    import ctypes as C
+
+    import torch
+
+    import nerf_b200 as nb
+    from nerf_b200 import abi
+
+    torch.cuda.set_device(0)
+    lib = abi.load()
+    stream = torch.cuda.current_stream()
+    h = C.c_void_p(stream.cuda_stream)
+    hbm, src = peaks()
+    tf_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) \
+        if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
+    l2 = l2_peaks(lib, stream)
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    reps = args.micro_reps
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3 / reps
+
+    def st(name, rc):
+        abi.check(name, rc)
+
+    out = {"encode": [], "mlp": [], "composite": []}
+    L = 16
+    for log2n in args.micro_points:
+        n = 1 << log2n
+        pos = torch.rand((n, 3), generator=gen, device="cuda", dtype=torch.float32)
+        feat = torch.empty((n, 2 * L), device="cuda", dtype=torch.float16)
+        dfeat = torch.randn((n, 2 * L), generator=gen, device="cuda", dtype=torch.float32).half()
+        for log2T in args.micro_tables:
+            g = nb.grid_layout(L, log2T, 16, 2048)
+            entries = int(g.offset[L])
+            table_mb = entries * 4 / 1e6
+            params = (torch.rand(2 * entries, generator=gen, device="cuda") * 2e-4 - 1e-4).half()
+            grad = torch.zeros(2 * entries, device="cuda", dtype=torch.float16)
+            tf = timed(lambda: st("grid_forward", lib.nerf_b200_grid_forward(
+                C.byref(g), pos.data_ptr(), n, params.data_ptr(), feat.data_ptr(), h)))
+            tb = timed(lambda: st("grid_backward", lib.nerf_b200_grid_backward(
+                C.byref(g), pos.data_ptr(), n, dfeat.data_ptr(), grad.data_ptr(), h)))
+            in_l2 = table_mb < 100.0
+            fwd_gbs, bwd_gbs = n * 588 / tf / 1e9, n * 1100 / tb / 1e9
+            red_gops = n * 128 / tb / 1e9
+            rec = {"points": n, "log2_T": log2T, "table_MB": table_mb, "fwd_ms": tf * 1e3, "bwd_ms": tb * 1e3,
+                   "fwd_gbs": fwd_gbs, "bwd_gbs": bwd_gbs, "bwd_corner_updates_g_per_s": red_gops,
+                   "bound": "L2" if in_l2 else "HBM",
+                   "fwd_frac": fwd_gbs / (l2["read_gbs"] if in_l2 else hbm),
+                   "bwd_frac": (red_gops / l2["red_f16x2_gops"]) if in_l2 else bwd_gbs / hbm}
+            if in_l2:
+                # Random points: per level and (y, z) corner pair, the x-pair is one 8-byte load when its entries
+                # form an aligned pair (1 case in 2) else two loads -> 96 sector reads per point; one 16-byte
+                # reduction when both entries share an aligned 4-entry block (3 in 4) else two -> 80 ops per point.
+                rec["fwd_l2_sector_frac"] = n * 96 * 32 / tf / 1e9 / l2["read_gbs"]
+                rec["bwd_l2_op_frac"] = n * 80 / tb / 1e9 / l2["red_v4_f16x2_gops"]
+            out["encode"].append(rec)
+            del params, grad
+        del pos, feat, dfeat
+    torch.cuda.empty_cache()
+
+    mlp = (torch.rand(10240, generator=gen, device="cuda") * 0.3 - 0.15).half()
+    parts = torch.zeros(int(lib.nerf_b200_field_backward_partial_floats()), device="cuda", dtype=torch.float32)
+    mg = torch.zeros(10240, device="cuda", dtype=torch.float32)
+    for log2n in args.micro_rows:
+        n = 1 << log2n
+        x = torch.randn((n, 32), generator=gen, device="cuda").half()
+        d = torch.randn((n, 3), generator=gen, device="cuda")
+        d = (d / d.norm(dim=1, keepdim=True)).contiguous()
+        raw = torch.empty((n, 4), device="cuda", dtype=torch.float32)
+        dout = torch.randn((n, 4), generator=gen, device="cuda") * 0.5
+        dx = torch.empty((n, 32), device="cuda", dtype=torch.float16)
+        tf = timed(lambda: st("mlp_forward", lib.nerf_b200_mlp_forward(
+            mlp.data_ptr(), x.data_ptr(), d.data_ptr(), n, raw.data_ptr(), h)))
+        tb = timed(lambda: st("mlp_backward", lib.nerf_b200_mlp_backward(
+            mlp.data_ptr(), x.data_ptr(), d.data_ptr(), n, dout.data_ptr(), dx.data_ptr(), parts.data_ptr(),
+            mg.data_ptr(), h)))
+        ff, fb = n * 20480 / tf / 1e12, n * 61440 / tb / 1e12
+        out["mlp"].append({"rows": n, "fwd_ms": tf * 1e3, "bwd_ms": tb * 1e3, "fwd_tflops": ff, "bwd_tflops": fb,
+                           "fwd_frac": ff / tf_peak, "bwd_frac": fb / tf_peak, "bound": "tensor"})
+        del x, d, raw, dout, dx
+    torch.cuda.empty_cache()
+
+    rays = 1 << 16
+    for S in args.micro_samples:
+        m = rays * S
+        rec = np.zeros((rays, 12), np.float32)
+        rec[:, 0] = 1.0
+        rec.view(np.uint32)[:, 3] = np.arange(rays, dtype=np.uint32) * S
+        rec[:, 4:8] = 0.5
+        rec[:, 8:11] = 1.0
+        rec.view(np.uint32)[:, 11] = S
+        rec_d = torch.from_numpy(rec).cuda()
+        sig = torch.empty(m, device="cuda").exponential_(1.0, generator=gen).clamp_min(1e-12)
+        col = torch.rand((m, 3), generator=gen, device="cuda").clamp(1e-6, 1 - 1e-6)
+        raw = torch.cat([sig.log()[:, None], torch.log(col / (1 - col))], dim=1).contiguous()
+        del sig, col
+        pos = torch.zeros((m, 4), device="cuda")
+        pos[:, 3] = 1.0 / S
+        dout = torch.empty((m, 4), device="cuda")
+        loss = torch.zeros(1, device="cuda")
+        t = timed(lambda: st("composite", lib.nerf_b200_composite(
+            rec_d.data_ptr(), rays, raw.data_ptr(), pos.data_ptr(), 1.0 / rays, 128.0, 0.0, dout.data_ptr(), None, None,
+            loss.data_ptr(), h)))
+        gbs = m * 88 / t / 1e9
+        out["composite"].append({"rays": rays, "samples_per_ray": S, "ms": t * 1e3, "gbs": gbs, "frac": gbs / hbm,
+                                 "bound": "HBM"})
+        del raw, pos, dout, rec_d
+    torch.cuda.empty_cache()
+    line = {"metric": "kernel microbench (config 5)", "unit": "see points", "n_gpus": 1, "reps": reps,
+            "peaks": {"hbm_gbs": hbm, "hbm_source": src, "bf16_tflops": tf_peak, "l2": l2},
+            "dtype": "f16 (fp32 accumulate)", "data": "synthetic", **out}
+    print(json.dumps(line), flush=True)
+
+
 # ------------------------------------------------------------ reference arm
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -522,14 +664,37 @@ def run_reference(args):
     for _ in range(args.warmup):
         pass
     res = cpu_baseline(nb, ds, args, steps=max(1, args.steps), threads=threads)
+    ref_cuda = None if args.skip_reference_cuda else reference_cuda(args)
     line = {"metric": "train samples/s (config 2, steady state)", "value": res["value"], "unit": "samples/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (fp16-rounded operands)", "data": "synthetic", "impl": "reference",
             "config": {"workload": WORKLOAD, "parallelism": "cpu"},
             "cpu_baseline": res,
-            "e2e": {"value": res["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "e2e": {"value": res["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_cuda": ref_cuda}
     print(json.dumps(line), flush=True)
+
+
+def reference_cuda(args):
+    """The reference's own CUDA backend (oracle/_ref/libref_stock.so: backend-cuda.cu built for sm_100a) through its
+    nerf.h on this GPU: config-2 training throughput, held-out PSNR and the config-3 render.  Runs in a child
+    process (the library exports the same nerf_* names as libnerf_b200.so) with a time limit."""
+    lib = ROOT / "oracle" / "_ref" / "libref_stock.so"
+    if not lib.exists():
+        return {"unavailable": "oracle/_ref/libref_stock.so is not built (the reference checkout was absent at build)"}
+    cmd = [sys.executable, "-m", "oracle.ref_backend", "--pretrain", str(args.pretrain), "--steps",
+           str(args.reference_cuda_steps), "--render-views", "4", "--psnr-views", "5", "--psnr-steps",
+           str(args.pretrain + 2 * args.warmup + args.steps)]  # the steps after which the own arm measures PSNR
+    try:
+        r = subprocess.run(cmd, cwd=str(ROOT), capture_output=True, text=True, timeout=900)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference backend run exceeded 900 s"}
+    lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+    if r.returncode != 0 or not lines:
+        tail = (r.stderr or r.stdout).strip().splitlines()[-1:] or ["no output"]
+        return {"unavailable": f"reference backend run failed (exit {r.returncode}): {tail[0][:300]}"}
+    return json.loads(lines[-1])
 
 
 def main():
@@ -547,10 +712,20 @@ def main():
     ap.add_argument("--skip-render", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-reference-cuda", action="store_true")
+    ap.add_argument("--micro", action="store_true", help="kernel microbench sweep (config 5) instead of the step")
+    ap.add_argument("--micro-reps", type=int, default=10)
+    ap.add_argument("--micro-points", type=int, nargs="*", default=[20, 22, 24])
+    ap.add_argument("--micro-tables", type=int, nargs="*", default=[14, 19, 22, 24])
+    ap.add_argument("--micro-rows", type=int, nargs="*", default=[16, 18, 20, 22])
+    ap.add_argument("--micro-samples", type=int, nargs="*", default=[1, 16, 64, 256, 1024])
+    ap.add_argument("--reference-cuda-steps", type=int, default=200)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.micro:
+        run_micro(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

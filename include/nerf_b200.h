@@ -209,6 +209,18 @@ NERF_API uint64_t nerf_b200_field_backward_partial_floats(void);
 NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, const void* params_f16, const float* pos_unit,
                                              const float* dirs, uint32_t n, const void* feat_f16, const float* dout,
                                              void* grid_grad_f16, float* partials, float* mlp_grad, void* stream);
+/* The two MLPs of the fused field alone, on given hash features (the
+ * encode skipped; used to measure the MLPs against the tensor-pipe roofline).
+ * mlp_params_f16: the 10240 MLP weights (the tail of the flat parameter
+ * vector); feat_f16: n x 32 fp16 features; dirs: n x 3 unit directions.
+ * Forward writes raw (n x 4).  Backward takes loss-scaled d raw (n x 4),
+ * writes the feature gradients dfeat_f16 (n x 32 fp16) and the 10240 weight
+ * gradients (partials as in nerf_b200_field_backward). */
+NERF_API NerfStatus nerf_b200_mlp_forward(const void* mlp_params_f16, const void* feat_f16, const float* dirs, uint32_t n,
+                                          float* raw, void* stream);
+NERF_API NerfStatus nerf_b200_mlp_backward(const void* mlp_params_f16, const void* feat_f16, const float* dirs, uint32_t n,
+                                           const float* dout, void* dfeat_f16, float* partials, float* mlp_grad,
+                                           void* stream);
 /* Allocation-free nerf_b200_field_backward (no counterpart in the reference).
  * For callers that cannot allocate device memory -- a plugin inside a host
  * application that owns the device memory budget, or code where a cudaMalloc

@@ -1491,6 +1491,45 @@ NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, c
     return nb::cuda_status(nb::launch_wgrad_reduce(o, s));
 }
 
+NERF_API NerfStatus nerf_b200_mlp_forward(const void* mlp_params, const void* feat, const float* dirs, uint32_t n, float* raw,
+                                          void* stream) {
+    if (n && (!mlp_params || !feat || !dirs || !raw)) return NERF_STATUS_INVALID_USAGE;
+    if (n == 0u) return NERF_STATUS_OK;
+    if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    nb::FieldArgs a{};
+    a.params16 = mlp_params;
+    a.mlp_offset = 0u;
+    a.n_direct = n;
+    a.dirs = dirs;
+    a.feat = const_cast<void*>(feat);
+    a.raw = reinterpret_cast<float4*>(raw);
+    return nb::cuda_status(nb::launch_field_forward(a, nb::kFieldMlp, nb::field_forward_blocks(), static_cast<cudaStream_t>(stream)));
+}
+
+NERF_API NerfStatus nerf_b200_mlp_backward(const void* mlp_params, const void* feat, const float* dirs, uint32_t n,
+                                           const float* dout, void* dfeat, float* partials, float* mlp_grad, void* stream) {
+    if (!mlp_params || !partials || !mlp_grad) return NERF_STATUS_INVALID_USAGE;
+    if (n && (!feat || !dirs || !dout || !dfeat)) return NERF_STATUS_INVALID_USAGE;
+    if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    nb::FieldArgs a{};
+    a.params16 = mlp_params;
+    a.mlp_offset = 0u;
+    a.n_direct = n;
+    a.dirs = dirs;
+    a.feat = const_cast<void*>(feat);
+    a.dout = reinterpret_cast<const float4*>(dout);
+    a.dfeat = dfeat;
+    a.partials = partials;
+    const uint32_t blocks = nb::field_backward_blocks();
+    if (nb::launch_field_backward(a, nb::kFieldMlp, blocks, s) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    nb::OptimArgs o{};
+    o.partials = partials;
+    o.n_partials = blocks;
+    o.mlp_grad = mlp_grad;
+    return nb::cuda_status(nb::launch_wgrad_reduce(o, s));
+}
+
 NERF_API NerfStatus nerf_b200_composite(const NerfB200RayRecord* rays, uint32_t n_rays, const float* raw, const float* pos_dt,
                                         float inv_norm, float loss_scale, float stop, float* dout, float* ray_loss,
                                         uint32_t* ray_used, float* loss_sum, void* stream) {

@@ -313,7 +313,7 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
         } else {
 #pragma unroll
             for (int k = 0; k < 3; ++k) {
-                u[k] = a.pos_unit[3ull * r + k];
+                if (mode == kFieldDirect) u[k] = a.pos_unit[3ull * r + k];
                 d[k] = a.dirs[3ull * r + k];
             }
         }
@@ -432,10 +432,19 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
         __syncthreads();  // this tile's stage is visible; the previous tile is done with shared memory
         load_rows(a, mode, s, &cur, row0, n);
         __syncthreads();
-        encode_rows(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
-                    [&](uint32_t r, const float4&) { return row0 + r < n; });
+        if (mode == kFieldMlp) {  // given features: 64-byte rows into feat[64][40]
+            const uint4* src = static_cast<const uint4*>(a.feat);
+            for (uint32_t c = threadIdx.x; c < kRows * 4u; c += kThreads) {
+                const uint32_t r = c >> 2, q = c & 3u;
+                const uint4 v = row0 + r < n ? src[static_cast<unsigned long long>(row0 + r) * 4u + q] : make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4*>(s.feat + r * kS32 + q * 8u) = v;
+            }
+        } else {
+            encode_rows(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
+                        [&](uint32_t r, const float4&) { return row0 + r < n; });
+        }
         __syncthreads();
-        if (mode != kFieldOccupancy && a.feat != nullptr) store_rows(a, s, mode, row0, n);
+        if ((mode == kFieldTrain || mode == kFieldDirect) && a.feat != nullptr) store_rows(a, s, mode, row0, n);
         const uint32_t wrow = warp * 16u;
         Chain c;
         forward_density(s.w, s.feat, wrow, lane, c);
@@ -511,7 +520,7 @@ __device__ __forceinline__ void bwd_prefetch(const FieldArgs& a, int mode, const
             const bool ok = row0 + r < n;
             cp_async16(st.feat + r * kS32 + q * 8u, gr + (ok ? static_cast<unsigned long long>(row0 + r) * 4u + q : 0ull), ok);
         }
-        if (tid >= kRows) {
+        if (mode == kFieldDirect && tid >= kRows) {
             const uint32_t i = tid - kRows, r = row0 + i;
             const bool ok = r < n;
             float* pp = reinterpret_cast<float*>(st.pos + i);
@@ -709,7 +718,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_field_backward(const FieldArgs 
             runs[(g + 8u) * kRunStride + 4u * nt + t] = __floats2half2_rn(dxd[nt][2], dxd[nt][3]);
         }
         __syncwarp();
-        if (mode == kFieldTrain) {
+        if (mode == kFieldTrain || mode == kFieldMlp) {
             uint32_t* df = static_cast<uint32_t*>(a.dfeat);
 #pragma unroll
             for (uint32_t k = 0; k < 8u; ++k) {
@@ -1008,7 +1017,7 @@ cudaError_t render_init_attributes() { return field_init_attributes(); }
 
 cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t blocks, cudaStream_t s) {
     if (blocks == 0u) return cudaErrorInvalidValue;
-    if (mode == kFieldTrain && a.dfeat == nullptr) return cudaErrorInvalidValue;
+    if ((mode == kFieldTrain || mode == kFieldMlp) && a.dfeat == nullptr) return cudaErrorInvalidValue;
     k_field_backward<<<blocks, kThreads, kBwdSmem, s>>>(a, mode);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || mode != kFieldTrain) return e;

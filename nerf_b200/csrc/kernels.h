@@ -26,7 +26,9 @@ cudaError_t launch_grid_backward(const LevelTable& lt, const float* pos_unit, ui
                                  void* grad_f16, cudaStream_t s);
 
 // ---- fused field (hash grid L=16 + density/colour MLPs) ----
-enum FieldMode : int { kFieldTrain = 0, kFieldOccupancy = 1, kFieldDirect = 2 };
+// kFieldMlp: the MLPs alone on given hash features (feat holds n x 32 fp16
+// input rows; forward writes raw, backward writes dfeat and weight gradients).
+enum FieldMode : int { kFieldTrain = 0, kFieldOccupancy = 1, kFieldDirect = 2, kFieldMlp = 3 };
 struct FieldArgs {
     LevelTable lt;
     const void* params16;   // flat fp16 parameters (grid entries, then MLP)
@@ -54,7 +56,8 @@ struct FieldArgs {
 };
 cudaError_t launch_field_forward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
 // Training mode: MLP backward writing dfeat, then the hash-table scatter
-// kernel.  Direct mode: one fused kernel (MLP backward + scatter).
+// kernel.  Direct mode: one fused kernel (MLP backward + scatter).  MLP mode:
+// the MLP backward writing dfeat, no scatter.
 cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
 uint32_t field_forward_blocks();
 uint32_t field_backward_blocks();

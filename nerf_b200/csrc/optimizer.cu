@@ -20,12 +20,29 @@
 namespace nb {
 namespace {
 
+// Sum over c = 0..n-1 of partials[c][i], added in order of c.  The loads of
+// 32 partials are issued before their adds, so a thread waits for one
+// memory round trip per 32 partials instead of one per partial (the order of
+// the additions, and so the result, is that of the plain loop).
+__device__ __forceinline__ float sum_partials(const float* __restrict__ partials, uint32_t n, uint32_t i) {
+    const float* p = partials + i;
+    float s = 0.0f;
+    uint32_t c = 0;
+    for (; c + 32u <= n; c += 32u) {
+        float v[32];
+#pragma unroll
+        for (uint32_t k = 0; k < 32u; ++k) v[k] = __ldcs(p + static_cast<unsigned long long>(c + k) * kMlpParams);
+#pragma unroll
+        for (uint32_t k = 0; k < 32u; ++k) s += v[k];
+    }
+    for (; c < n; ++c) s += __ldcs(p + static_cast<unsigned long long>(c) * kMlpParams);
+    return s;
+}
+
 __global__ void __launch_bounds__(256) k_wgrad_reduce(const float* __restrict__ partials, uint32_t n_partials, float* mlp_grad) {
     const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= kMlpParams) return;
-    float s = 0.0f;
-    for (uint32_t c = 0; c < n_partials; ++c) s += partials[static_cast<unsigned long long>(c) * kMlpParams + i];
-    mlp_grad[i] = s;
+    mlp_grad[i] = sum_partials(partials, n_partials, i);
 }
 
 __device__ __forceinline__ void adam_scalars(const TrainConsts& tc, float grad_norm, uint32_t nonfinite, uint32_t step,
@@ -65,8 +82,7 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
         if (blockIdx.x < kWgradBlocks) {
             const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
             if (i < kMlpParams) {
-                float g = 0.0f;
-                for (uint32_t c = 0; c < a.n_partials; ++c) g += a.partials[static_cast<unsigned long long>(c) * kMlpParams + i];
+                const float g = sum_partials(a.partials, a.n_partials, i);
                 a.mlp_grad[i] = g;
                 if (!isfinite(g)) bad = 1u;
                 else sum = g * g;

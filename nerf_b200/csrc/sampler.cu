@@ -14,9 +14,10 @@
 //                  bit word, its popcount is added to the ray's count;
 //   k_sample_scan  ordered exclusive scans of counts and active flags with
 //                  the capacity cut;
-//   k_sample_write one warp per kept ray: samples at their final offsets
-//                  (chunk offsets from a warp scan of the bit-word counts),
-//                  then the ray record with its ground-truth colour.
+//   k_sample_write one warp per kept ray: samples at their final offsets,
+//                  one sample per lane (chunk from a warp scan of the
+//                  bit-word counts, step from the set bit of its rank), then
+//                  the ray record with its ground-truth colour.
 // All float arithmetic that decides which steps are kept uses explicit
 // rounding intrinsics, so the CPU oracle reproduces per-ray counts and
 // offsets bit for bit.  (The reference normalises with the approximate
@@ -304,9 +305,30 @@ __device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom
     a.rays[slot] = rec;
 }
 
+// Position of the set bit of rank `rank` (0-based, from bit 0) in `bits`,
+// which has more than `rank` set bits: a binary search over bit positions
+// with population counts of the lower half of the remaining window.
+__device__ __forceinline__ uint32_t select_bit(uint32_t bits, uint32_t rank) {
+    uint32_t pos = 0u;
+#pragma unroll
+    for (uint32_t w = 16u; w > 0u; w >>= 1) {
+        const uint32_t low = static_cast<uint32_t>(__popc(bits & ((1u << w) - 1u)));
+        if (rank >= low) {
+            rank -= low;
+            bits >>= w;
+            pos += w;
+        }
+    }
+    return pos;
+}
+
 // One warp per kept ray (grid-stride).  Lane k holds the bit word of chunk
-// 32q+k; a warp scan of their counts gives each chunk's offset, and lane j
-// of a chunk with samples writes step 32c+j at its rank among the set bits.
+// 32q+k and a warp scan gives the chunks' inclusive sample counts.  Then each
+// lane writes one sample at a time: sample s of the group lies in the first
+// chunk whose inclusive count exceeds s (binary search over the 32 counts
+// with shuffles) at the set bit of rank s - (samples of the earlier chunks).
+// Consecutive lanes write consecutive samples, and each round's step loads
+// are independent, so a ray costs one memory round trip per 32 samples.
 __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     const uint32_t frame = a.state->frame_index;
@@ -333,22 +355,25 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
                 const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= static_cast<uint32_t>(o)) incl += x;
             }
-            const uint32_t base = out + incl - cnt;
-            uint32_t todo = __ballot_sync(0xffffffffu, mine != 0u);
-            while (todo) {
-                const uint32_t k = static_cast<uint32_t>(__ffs(todo)) - 1u;
-                todo &= todo - 1u;
+            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+            for (uint32_t sb = 0; sb < total; sb += 32u) {
+                const uint32_t si = sb + lane;
+                uint32_t k = 0u;  // chunks whose inclusive count is <= si (at most 31)
+#pragma unroll
+                for (uint32_t step = 16u; step > 0u; step >>= 1) {
+                    const uint32_t v = __shfl_sync(0xffffffffu, incl, k + step - 1u);
+                    if (v <= si) k += step;
+                }
                 const uint32_t bits = __shfl_sync(0xffffffffu, mine, k);
-                const uint32_t at = __shfl_sync(0xffffffffu, base, k);
-                if ((bits >> lane) & 1u) {
+                const uint32_t first = __shfl_sync(0xffffffffu, incl, k) - static_cast<uint32_t>(__popc(bits));
+                if (si < total) {
                     float p[3];
-                    const float dt = step_point(a, g, r, 32u * (c0 + k) + lane, p);
-                    const uint32_t o = at + __popc(bits & ((1u << lane) - 1u));
-                    a.pos_dt[o] = make_float4(p[0], p[1], p[2], dt);
-                    a.sample_ray[o] = slot;
+                    const float dt = step_point(a, g, r, 32u * (c0 + k) + select_bit(bits, si - first), p);
+                    a.pos_dt[out + si] = make_float4(p[0], p[1], p[2], dt);
+                    a.sample_ray[out + si] = slot;
                 }
             }
-            out += __shfl_sync(0xffffffffu, incl, 31);
+            out += total;
         }
         if (lane == 0u) write_record(a, g, r, slot, excl, count, frame, camera);
     }

@@ -17,6 +17,9 @@
 //                                            backend-cuda.cu:1555-1634
 //   hashing      nerf::sampler hash_u32 / rand01 (:321-332), nerf::runtime
 //                hash_u32 (:1439-1446)
+// and two timing loops around the reference's own public entry points
+// (nerf_train_step :2405-2420, nerf_inference :2436-2466), which give the
+// reference-backend baseline of the training and render throughput.
 //
 // NERF_REF_PARITY builds a second variant in which the reference's
 // approximate rsqrtf (used once, for the ray direction, :384) is replaced by
@@ -53,6 +56,19 @@ __global__ void k_ref_hash(const std::uint32_t* in, std::uint32_t* out_sampler, 
 }
 
 int status(cudaError_t e) { return e == cudaSuccess ? 0 : static_cast<int>(e); }
+
+// Adds one step's compacted sample count and kept ray count to acc[0], acc[1]
+// (the reference exports no sample counter; this reads its SampleBatchState).
+__global__ void k_ref_count_batch(const nerf::sampler::SampleBatchState* batch, unsigned long long* acc) {
+    acc[0] += batch->sample_step_count;
+    acc[1] += batch->active_ray_count;
+}
+
+nerf::runtime::TrainRuntime* ref_runtime(void* context) {
+    auto* ctx = static_cast<nerf::runtime::ContextStorage*>(context);
+    if (!ctx || !ctx->cuda_context) return nullptr;
+    return ctx->cuda_context->train_runtime.get();
+}
 
 }  // namespace
 
@@ -183,6 +199,82 @@ int ref_occupancy(std::uint32_t frame, std::uint32_t mode, void* d_state, float*
     }
     nerf::runtime::k_rebuild_occ_from_density<<<(cells + 255u) / 256u, 256u>>>(d_density, s, cells, threshold, d_bitfield);
     return status(cudaDeviceSynchronize());
+}
+
+// The last CUDA runtime error of the calling thread (cudaGetLastError: the
+// reference's entry points report a failed runtime call only as a status),
+// its name copied into name[len].
+int ref_last_cuda_error(char* name, std::uint32_t len) {
+    const cudaError_t e = cudaGetLastError();
+    if (name && len) {
+        const char* s = cudaGetErrorName(e);
+        std::uint32_t i = 0;
+        for (; s && s[i] && i + 1 < len; ++i) name[i] = s[i];
+        name[i] = 0;
+    }
+    return static_cast<int>(e);
+}
+
+// The reference's own training step, timed: `steps` calls of its
+// nerf_train_step (one graph launch each on the context's stream) between two
+// CUDA events on that stream.  After every step a one-thread kernel adds the
+// step's compacted sample and kept-ray counts to a device accumulator, so
+// samples/s covers exactly the timed steps (about 2 us per step of the timed
+// region is this counter).  out: {samples, rays}; *ms: device time.
+int ref_train_timed(void* context, std::uint32_t steps, float* ms, std::uint64_t out[2]) {
+    nerf::runtime::TrainRuntime* rt = ref_runtime(context);
+    if (!rt || !rt->training_configured || !ms || !out) return -1;
+    auto* ctx = static_cast<nerf::runtime::ContextStorage*>(context);
+    const auto* batch = reinterpret_cast<const nerf::sampler::SampleBatchState*>(ctx->sample_batch_state.ptr);
+    unsigned long long* acc = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaMalloc(&acc, 2 * sizeof(unsigned long long));
+    if (e == cudaSuccess) e = cudaMemsetAsync(acc, 0, 2 * sizeof(unsigned long long), rt->stream);
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, rt->stream);
+    int rc = 0;
+    for (std::uint32_t i = 0; e == cudaSuccess && rc == 0 && i < steps; ++i) {
+        rc = static_cast<int>(nerf_train_step(context));
+        if (rc == 0) {
+            k_ref_count_batch<<<1, 1, 0, rt->stream>>>(batch, acc);
+            e = cudaGetLastError();
+        }
+    }
+    if (e == cudaSuccess && rc == 0) e = cudaEventRecord(e1, rt->stream);
+    if (e == cudaSuccess && rc == 0) e = cudaEventSynchronize(e1);
+    if (e == cudaSuccess && rc == 0) e = cudaEventElapsedTime(ms, e0, e1);
+    unsigned long long h[2] = {0, 0};
+    if (e == cudaSuccess && rc == 0) e = cudaMemcpy(h, acc, sizeof(h), cudaMemcpyDeviceToHost);
+    out[0] = h[0];
+    out[1] = h[1];
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (acc) cudaFree(acc);
+    return rc != 0 ? 1000 + rc : status(e);
+}
+
+// The reference's nerf_inference of dataset camera `camera_idx` at
+// `samples_per_ray` uniform samples, timed with CUDA events on the context's
+// stream (dst NULL: the image stays in the context's device buffer).
+int ref_inference_timed(void* context, std::uint32_t camera_idx, std::uint32_t samples_per_ray, float* ms) {
+    nerf::runtime::TrainRuntime* rt = ref_runtime(context);
+    if (!rt || !ms) return -1;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    cudaError_t e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    if (e == cudaSuccess) e = cudaEventRecord(e0, rt->stream);
+    int rc = 0;
+    if (e == cudaSuccess) {
+        NerfInferenceRequest req{camera_idx, samples_per_ray, NERF_MEMORY_CUDA_DEVICE, nullptr, 0};
+        rc = static_cast<int>(nerf_inference(context, &req, nullptr));
+    }
+    if (e == cudaSuccess && rc == 0) e = cudaEventRecord(e1, rt->stream);
+    if (e == cudaSuccess && rc == 0) e = cudaEventSynchronize(e1);
+    if (e == cudaSuccess && rc == 0) e = cudaEventElapsedTime(ms, e0, e1);
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    return rc != 0 ? 1000 + rc : status(e);
 }
 
 }  // extern "C"

@@ -145,6 +145,47 @@ def test_field_backward_matches_oracle(cuda):
     assert np.linalg.norm(got_g - want_g) / np.linalg.norm(want_g) < 2e-2
 
 
+def test_mlp_only_matches_fused_field(cuda):
+    """The MLP-only entry points on the hash features of the fused field give the fused field's raw outputs and
+    weight gradients bit for bit (same tiles, same fragments, same fixed-order reduction), and feature gradients
+    that scattered by the standalone grid backward match the fused scatter within fp16 reduction order."""
+    torch = cuda
+    lib = abi.load()
+    rng = np.random.default_rng(9)
+    n = 3001
+    g, og, params, pos, dirs = _field_setup(rng, n=n)
+    n_grid = 2 * g.offset[16]
+    par_d, pos_d, dir_d = dev(torch, params), dev(torch, pos), dev(torch, dirs)
+    mlp_ptr = par_d.data_ptr() + 2 * n_grid
+    feat_d, raw_d, raw2_d = zeros(torch, (n, 32), np.uint16), zeros(torch, (n, 4), np.float32), zeros(torch, (n, 4), np.float32)
+    check("field_forward", lib.nerf_b200_field_forward(C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), n,
+                                                       feat_d.data_ptr(), raw_d.data_ptr(), None))
+    check("mlp_forward", lib.nerf_b200_mlp_forward(mlp_ptr, feat_d.data_ptr(), dir_d.data_ptr(), n, raw2_d.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert np.array_equal(host(raw_d).view(np.uint32), host(raw2_d).view(np.uint32))
+
+    dout_d = dev(torch, (rng.standard_normal((n, 4)) * 0.5).astype(np.float32))
+    parts = int(lib.nerf_b200_field_backward_partial_floats())
+    gg_d, part_d, mg_d = zeros(torch, n_grid, np.uint16), zeros(torch, parts, np.float32), zeros(torch, 10240, np.float32)
+    check("field_backward", lib.nerf_b200_field_backward(
+        C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), n, feat_d.data_ptr(), dout_d.data_ptr(),
+        gg_d.data_ptr(), part_d.data_ptr(), mg_d.data_ptr(), None))
+    dfeat_d, part2_d, mg2_d = zeros(torch, (n, 32), np.uint16), zeros(torch, parts, np.float32), zeros(torch, 10240, np.float32)
+    check("mlp_backward", lib.nerf_b200_mlp_backward(mlp_ptr, feat_d.data_ptr(), dir_d.data_ptr(), n, dout_d.data_ptr(),
+                                                     dfeat_d.data_ptr(), part2_d.data_ptr(), mg2_d.data_ptr(), None))
+    gg2_d = zeros(torch, n_grid, np.uint16)
+    check("grid_backward", lib.nerf_b200_grid_backward(C.byref(g), pos_d.data_ptr(), n, dfeat_d.data_ptr(), gg2_d.data_ptr(),
+                                                       None))
+    torch.cuda.synchronize()
+    assert np.array_equal(host(mg_d).view(np.uint32), host(mg2_d).view(np.uint32))
+    a = host(gg_d, np.uint16).view(np.float16).astype(np.float64)
+    b = host(gg2_d, np.uint16).view(np.float16).astype(np.float64)
+    assert np.linalg.norm(a - b) / np.linalg.norm(a) < 5e-3
+    # invalid use: missing feature-gradient output
+    assert lib.nerf_b200_mlp_backward(mlp_ptr, feat_d.data_ptr(), dir_d.data_ptr(), n, dout_d.data_ptr(), None,
+                                      part2_d.data_ptr(), mg2_d.data_ptr(), None) == abi.NERF_STATUS_INVALID_USAGE
+
+
 def _records(begin, count, gt, bg, dirs):
     n = len(begin)
     rec = np.zeros((n, 12), np.float32)

@@ -163,3 +163,12 @@ def test_occupancy_update_against_reference(ref, mode):
     if mode == 2:
         pos = oracle.occupancy_cells(frame, update, cells, OCC_GRID, AABB[0], AABB[1])
         assert np.array_equal(pos.view(np.uint32), d[f"occ_m{mode}_inputs"][:, :3].view(np.uint32)), "query cells"
+
+
+def test_reference_harness_exports_timing_loops():
+    """The reference-backend timing loops (bench.py's reference arm) are exported by the harness build."""
+    lib = GOLDEN.parents[1] / "oracle" / "_ref" / "libref_stock.so"
+    if not lib.exists():
+        pytest.skip("reference harness not built (reference checkout absent at build time)")
+    from oracle import ref_backend
+    ref_backend.load()  # declares every entry point; AttributeError if one is missing
