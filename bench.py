@@ -612,12 +612,22 @@ def run_micro(args):
         dx = torch.empty((n, 32), device="cuda", dtype=torch.float16)
         tf = timed(lambda: st("mlp_forward", lib.nerf_b200_mlp_forward(
             mlp.data_ptr(), x.data_ptr(), d.data_ptr(), n, raw.data_ptr(), h)))
+        err = torch.zeros(1, device="cuda", dtype=torch.int32)
+        ttc = timed(lambda: st("mlp_forward_tc", lib.nerf_b200_mlp_forward_tc(
+            mlp.data_ptr(), x.data_ptr(), d.data_ptr(), n, raw.data_ptr(), err.data_ptr(), h)))
         tb = timed(lambda: st("mlp_backward", lib.nerf_b200_mlp_backward(
             mlp.data_ptr(), x.data_ptr(), d.data_ptr(), n, dout.data_ptr(), dx.data_ptr(), parts.data_ptr(),
             mg.data_ptr(), h)))
-        ff, fb = n * 20480 / tf / 1e12, n * 61440 / tb / 1e12
+        tbc = timed(lambda: st("mlp_backward_tc", lib.nerf_b200_mlp_backward_tc(
+            mlp.data_ptr(), x.data_ptr(), d.data_ptr(), n, dout.data_ptr(), dx.data_ptr(), parts.data_ptr(),
+            mg.data_ptr(), err.data_ptr(), h)))
+        ff, fb, ftc = n * 20480 / tf / 1e12, n * 61440 / tb / 1e12, n * 20480 / ttc / 1e12
+        fbc = n * 61440 / tbc / 1e12
         out["mlp"].append({"rows": n, "fwd_ms": tf * 1e3, "bwd_ms": tb * 1e3, "fwd_tflops": ff, "bwd_tflops": fb,
-                           "fwd_frac": ff / tf_peak, "bwd_frac": fb / tf_peak, "bound": "tensor"})
+                           "fwd_frac": ff / tf_peak, "bwd_frac": fb / tf_peak, "fwd_tc_ms": ttc * 1e3,
+                           "fwd_tc_tflops": ftc, "fwd_tc_frac": ftc / tf_peak, "bwd_tc_ms": tbc * 1e3,
+                           "bwd_tc_tflops": fbc, "bwd_tc_frac": fbc / tf_peak, "tc_error_word": int(err.item()),
+                           "bound": "tensor"})
         del x, d, raw, dout, dx
     torch.cuda.empty_cache()
 
@@ -647,6 +657,10 @@ def run_micro(args):
                                  "bound": "HBM"})
         del raw, pos, dout, rec_d
     torch.cuda.empty_cache()
+    info = (C.c_uint32 * 4)()
+    lib.nerf_b200_mlp_tc_info(info)
+    out["mlp_tc_launch"] = {"fwd_grid": info[0], "bwd_grid": info[1], "runtime_occupancy_fwd": info[2],
+                            "runtime_occupancy_bwd": info[3]}
     line = {"metric": "kernel microbench (config 5)", "unit": "see points", "n_gpus": 1, "reps": reps,
             "peaks": {"hbm_gbs": hbm, "hbm_source": src, "bf16_tflops": tf_peak, "l2": l2},
             "dtype": "f16 (fp32 accumulate)", "data": "synthetic", **out}

@@ -218,6 +218,24 @@ NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, c
  * gradients (partials as in nerf_b200_field_backward). */
 NERF_API NerfStatus nerf_b200_mlp_forward(const void* mlp_params_f16, const void* feat_f16, const float* dirs, uint32_t n,
                                           float* raw, void* stream);
+/* nerf_b200_mlp_forward on the 5th-generation tensor cores (tcgen05.mma with
+ * tensor-memory accumulators, 128-row tiles).  error_word: one device uint32;
+ * bit 0 is set when a CTA's MMAs did not complete within a second (the CTA
+ * then stops; its rows of raw are not written). */
+NERF_API NerfStatus nerf_b200_mlp_forward_tc(const void* mlp_params_f16, const void* feat_f16, const float* dirs, uint32_t n,
+                                             float* raw, uint32_t* error_word, void* stream);
+/* nerf_b200_mlp_backward on tcgen05: per 128-row tile the forward is
+ * recomputed, each backward layer's input-gradient MMA and weight-gradient MMA
+ * read the same shared-memory operands, and the weight gradients accumulate
+ * in tensor memory across the CTA's tiles.  Same outputs and partials contract
+ * as nerf_b200_mlp_backward; error_word as in nerf_b200_mlp_forward_tc. */
+/* Launch geometry of the tensor-core MLP kernels: out[0] / out[1] persistent
+ * grid of the forward / backward (CTAs), out[2] / out[3] the CUDA runtime's
+ * occupancy answer for them (CTAs per SM). */
+NERF_API NerfStatus nerf_b200_mlp_tc_info(uint32_t out[4]);
+NERF_API NerfStatus nerf_b200_mlp_backward_tc(const void* mlp_params_f16, const void* feat_f16, const float* dirs, uint32_t n,
+                                              const float* dout, void* dfeat_f16, float* partials, float* mlp_grad,
+                                              uint32_t* error_word, void* stream);
 NERF_API NerfStatus nerf_b200_mlp_backward(const void* mlp_params_f16, const void* feat_f16, const float* dirs, uint32_t n,
                                            const float* dout, void* dfeat_f16, float* partials, float* mlp_grad,
                                            void* stream);

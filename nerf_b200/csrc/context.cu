@@ -232,6 +232,7 @@ struct Context {
     float* partials = nullptr;
     float* occ_sigma = nullptr;
     uint32_t n_partials = 0, fwd_blocks = 0;
+    bool mlp_tc = false;  // training backward MLP on tcgen05 (NERF_B200_MLP_TC)
     // render
     uint32_t* render_rgba = nullptr;
     uint32_t* render_counter = nullptr;
@@ -495,7 +496,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     t.lr_decay_ksteps = c.hyper_params.lr_decay_ksteps;
 
     // batch arena
-    n_partials = field_backward_blocks();
+    mlp_tc = env_u32("NERF_B200_MLP_TC", 0u) != 0u && mlp_backward_tc_blocks() != 0u;
+    n_partials = mlp_tc ? mlp_backward_tc_blocks() : field_backward_blocks();
     fwd_blocks = field_forward_blocks();
     batch.align = model.align;
     batch.size = 0;
@@ -651,9 +653,25 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = launch_field_forward(occq, kFieldOccupancy, fwd_blocks, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_occupancy_update(oa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_sampler(sa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if ((e = launch_field_forward(fa, kFieldTrain, fwd_blocks, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    if (mlp_tc) {  // encode + SH into the training rows, then the MLPs on tcgen05
+        if ((e = launch_field_encode(fa, s)) != cudaSuccess ||
+            (e = launch_mlp_forward_tc_train(p16 + n_grid, feat, &state->n_samples, reinterpret_cast<float*>(raw), &state->mlp_error,
+                                             s)) != cudaSuccess)
+            return e;
+    } else if ((e = launch_field_forward(fa, kFieldTrain, fwd_blocks, s)) != cudaSuccess) {
+        return e;
+    }
+    if ((e = mark()) != cudaSuccess) return e;
     if ((e = launch_composite(ca, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if ((e = launch_field_backward(fa, kFieldTrain, n_partials, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    if (mlp_tc) {  // MLP backward on tcgen05 (writes the feature gradients), then the hash-table scatter
+        if ((e = launch_mlp_backward_tc(p16 + n_grid, feat, 1, nullptr, reinterpret_cast<const float*>(dout), &state->n_samples, 0u,
+                                        dfeat, partials, n_partials, &state->mlp_error, s)) != cudaSuccess ||
+            (e = launch_grid_scatter(fa, s)) != cudaSuccess)
+            return e;
+    } else if ((e = launch_field_backward(fa, kFieldTrain, n_partials, s)) != cudaSuccess) {
+        return e;
+    }
+    if ((e = mark()) != cudaSuccess) return e;
     // One GPU: the statistics kernel also reduces the weight-gradient partials.
     op.fuse_wgrad = comm ? 0u : 1u;
     if (!op.fuse_wgrad && (e = launch_wgrad_reduce(op, s)) != cudaSuccess) return e;
@@ -1092,13 +1110,15 @@ NERF_API NerfStatus nerf_read_train_stats(void* context, NerfTrainStats* out) {
     std::lock_guard<std::mutex> lk(c->mu);
     if (!c->configured) return NERF_STATUS_STATE_ERROR;
     NB_TRY(cudaMemcpyAsync(out, &c->state->stats, sizeof(NerfTrainStats), cudaMemcpyDeviceToHost, c->stream));
-    uint32_t dp_error = 0u;
+    uint32_t dp_error = 0u, mlp_error = 0u;
     if (c->dp_peer) NB_TRY(cudaMemcpyAsync(&dp_error, &c->dp_sync->error, 4, cudaMemcpyDeviceToHost, c->stream));
+    if (c->mlp_tc) NB_TRY(cudaMemcpyAsync(&mlp_error, &c->state->mlp_error, 4, cudaMemcpyDeviceToHost, c->stream));
     NB_TRY(cudaStreamSynchronize(c->stream));
     c->host_generation = out->completed_steps;
     // A data-parallel barrier that timed out (a rank stopped stepping): the
-    // replicas are no longer in step.
-    return dp_error ? NERF_STATUS_CUDA_ERROR : NERF_STATUS_OK;
+    // replicas are no longer in step.  A tensor-core MLP kernel whose MMAs did
+    // not complete: the step's gradients are incomplete.
+    return (dp_error || mlp_error) ? NERF_STATUS_CUDA_ERROR : NERF_STATUS_OK;
 }
 
 NERF_API NerfStatus nerf_inference(void* context, const NerfInferenceRequest* req, NerfInferenceInfo* info) {
@@ -1504,6 +1524,39 @@ NERF_API NerfStatus nerf_b200_mlp_forward(const void* mlp_params, const void* fe
     a.feat = const_cast<void*>(feat);
     a.raw = reinterpret_cast<float4*>(raw);
     return nb::cuda_status(nb::launch_field_forward(a, nb::kFieldMlp, nb::field_forward_blocks(), static_cast<cudaStream_t>(stream)));
+}
+
+NERF_API NerfStatus nerf_b200_mlp_forward_tc(const void* mlp_params, const void* feat, const float* dirs, uint32_t n, float* raw,
+                                             uint32_t* error_word, void* stream) {
+    if (n && (!mlp_params || !feat || !dirs || !raw || !error_word)) return NERF_STATUS_INVALID_USAGE;
+    if (n == 0u) return NERF_STATUS_OK;
+    return nb::cuda_status(nb::launch_mlp_forward_tc(mlp_params, feat, dirs, n, raw, error_word, static_cast<cudaStream_t>(stream)));
+}
+
+NERF_API NerfStatus nerf_b200_mlp_tc_info(uint32_t out[4]) {
+    if (!out) return NERF_STATUS_INVALID_USAGE;
+    nb::mlp_tc_info(out);
+    return out[0] ? NERF_STATUS_OK : NERF_STATUS_CUDA_ERROR;
+}
+
+NERF_API NerfStatus nerf_b200_mlp_backward_tc(const void* mlp_params, const void* feat, const float* dirs, uint32_t n,
+                                              const float* dout, void* dfeat, float* partials, float* mlp_grad, uint32_t* error_word,
+                                              void* stream) {
+    if (!mlp_params || !partials || !mlp_grad || !error_word) return NERF_STATUS_INVALID_USAGE;
+    if (n && (!feat || !dirs || !dout || !dfeat)) return NERF_STATUS_INVALID_USAGE;
+    if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    const cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint32_t cap = nb::mlp_backward_tc_blocks();
+    if (cap == 0u || cap > nb::field_backward_blocks()) return NERF_STATUS_CUDA_ERROR;  // partials sized for the field backward
+    const uint32_t tiles = (n + 127u) / 128u;
+    const uint32_t blocks = tiles == 0u ? 1u : (tiles < cap ? tiles : cap);
+    if (nb::launch_mlp_backward_tc(mlp_params, feat, 0, dirs, dout, nullptr, n, dfeat, partials, blocks, error_word, s) != cudaSuccess)
+        return NERF_STATUS_CUDA_ERROR;
+    nb::OptimArgs o{};
+    o.partials = partials;
+    o.n_partials = blocks;
+    o.mlp_grad = mlp_grad;
+    return nb::cuda_status(nb::launch_wgrad_reduce(o, s));
 }
 
 NERF_API NerfStatus nerf_b200_mlp_backward(const void* mlp_params, const void* feat, const float* dirs, uint32_t n,

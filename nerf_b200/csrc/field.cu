@@ -467,6 +467,51 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
     cp_async_wait<0>();
 }
 
+// Training forward without the MLPs (the tensor-core MLP kernel of mlp_tc.cu
+// evaluates them from the rows written here): hash encode and SH of 64-row
+// tiles, written as the 112-byte training rows.  No weights in shared memory,
+// so more CTAs are resident to hide the gathers' latency.
+constexpr size_t kEncBase = (2 * kRows * kS32) * 2 + kRows * 16 + kMaxLevels * 16;
+constexpr size_t kEncSmem = kEncBase + 2 * kFwdStage;
+
+__global__ void __launch_bounds__(kThreads) k_field_encode(const FieldArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Smem s{};
+    s.w = nullptr;
+    s.feat = reinterpret_cast<__half*>(smem_raw);
+    s.xc = s.feat + kRows * kS32;
+    s.pos = reinterpret_cast<float4*>(s.xc + kRows * kS32);
+    s.lv = reinterpret_cast<LevelParams*>(s.pos + kRows);
+    auto stage = [&](uint32_t k) {
+        FwdStage st;
+        st.pos = reinterpret_cast<float4*>(smem_raw + kEncBase + k * kFwdStage);
+        st.sray = reinterpret_cast<uint32_t*>(st.pos + kRows);
+        return st;
+    };
+    const uint32_t n = a.state->n_samples;
+    if (n == 0u) return;
+    load_levels(a.lt, s.lv);
+    const uint32_t n_tiles = (n + kRows - 1u) / kRows;
+    if (blockIdx.x < n_tiles) fwd_prefetch(a, stage(0), blockIdx.x * kRows, n);
+    cp_async_commit();
+    uint32_t it = 0;
+    for (uint32_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+        const uint32_t row0 = tile * kRows;
+        const FwdStage cur = stage(it & 1u);
+        if (tile + gridDim.x < n_tiles) fwd_prefetch(a, stage((it + 1u) & 1u), (tile + gridDim.x) * kRows, n);
+        cp_async_commit();
+        cp_async_wait<1>();
+        __syncthreads();  // this tile's stage is visible; the previous tile's rows are stored
+        load_rows(a, kFieldTrain, s, &cur, row0, n);
+        __syncthreads();
+        encode_rows(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
+                    [&](uint32_t r, const float4&) { return row0 + r < n; });
+        __syncthreads();
+        store_rows(a, s, kFieldTrain, row0, n);
+    }
+    cp_async_wait<0>();
+}
+
 // ---- weight-gradient ownership: warp w accumulates 20 m16n8 tiles ----
 // acc[NT] += (A_s^T)[m0:m0+16, rows] x B_s[rows, n0:n0+8NT] over the tile's 64 rows.
 template <int NT>
@@ -977,7 +1022,7 @@ __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
 
 uint32_t g_render_blocks = 0;
 
-uint32_t g_fwd_blocks = 0, g_bwd_blocks = 0;
+uint32_t g_fwd_blocks = 0, g_bwd_blocks = 0, g_enc_blocks = 0;
 
 }  // namespace
 
@@ -997,6 +1042,11 @@ cudaError_t field_init_attributes() {
     int r = 0;
     if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, k_render, kThreads, kRenderSmem)) != cudaSuccess) return e;
     g_render_blocks = static_cast<uint32_t>(sms * (r > 0 ? r : 1));
+    e = cudaFuncSetAttribute(k_field_encode, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kEncSmem));
+    if (e != cudaSuccess) return e;
+    int en = 0;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&en, k_field_encode, kThreads, kEncSmem)) != cudaSuccess) return e;
+    g_enc_blocks = static_cast<uint32_t>(sms * (en > 0 ? en : 1));
     g_bwd_blocks = static_cast<uint32_t>(sms * (b > 0 ? b : 1));
     return cudaSuccess;
 }
@@ -1006,6 +1056,11 @@ uint32_t field_backward_blocks() { return g_bwd_blocks; }
 cudaError_t launch_field_forward(const FieldArgs& a, int mode, uint32_t blocks, cudaStream_t s) {
     if (blocks == 0u) return cudaErrorInvalidValue;
     k_field_forward<<<blocks, kThreads, kFwdSmem, s>>>(a, mode);
+    return cudaGetLastError();
+}
+cudaError_t launch_field_encode(const FieldArgs& a, cudaStream_t s) {
+    if (g_enc_blocks == 0u || a.feat == nullptr) return cudaErrorInvalidValue;
+    k_field_encode<<<g_enc_blocks, kThreads, kEncSmem, s>>>(a);
     return cudaGetLastError();
 }
 cudaError_t launch_render(const RenderArgs& a, cudaStream_t s) {
@@ -1021,8 +1076,14 @@ cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t blocks,
     k_field_backward<<<blocks, kThreads, kBwdSmem, s>>>(a, mode);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || mode != kFieldTrain) return e;
+    return launch_grid_scatter(a, s);
+}
+
+cudaError_t launch_grid_scatter(const FieldArgs& a, cudaStream_t s) {
+    if (a.dfeat == nullptr || a.grid_grad == nullptr) return cudaErrorInvalidValue;
     int dev = 0, sms = 148;
-    if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
     k_grid_scatter<<<static_cast<uint32_t>(sms) * 8u, kScatterThreads, 0, s>>>(a);
     return cudaGetLastError();

@@ -59,9 +59,39 @@ cudaError_t launch_field_forward(const FieldArgs& a, int mode, uint32_t grid_blo
 // kernel.  Direct mode: one fused kernel (MLP backward + scatter).  MLP mode:
 // the MLP backward writing dfeat, no scatter.
 cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
+// Training forward without the MLPs: hash encode + SH of a.state->n_samples
+// rows into the 112-byte training rows a.feat (launch_mlp_forward_tc_train
+// then evaluates the MLPs).
+cudaError_t launch_field_encode(const FieldArgs& a, cudaStream_t s);
+// The hash-table scatter of the training backward alone (feature gradients
+// in a.dfeat, positions in the training rows a.feat, a.state->n_samples rows).
+cudaError_t launch_grid_scatter(const FieldArgs& a, cudaStream_t s);
 uint32_t field_forward_blocks();
 uint32_t field_backward_blocks();
 cudaError_t field_init_attributes();
+
+// ---- the field MLPs on tcgen05 (mlp_tc.cu) ----
+// Forward of the MLPs on given features (n x 32 fp16) and directions, raw
+// (n x 4) out; *error gets bit 0 when a CTA's MMAs did not complete in time.
+cudaError_t launch_mlp_forward_tc(const void* mlp, const void* feat, const float* dirs, uint32_t n, float* raw, uint32_t* error,
+                                  cudaStream_t s);
+// Forward over the 112-byte training rows of the field forward (n read from
+// *n_device), raw (n x 4) out.
+cudaError_t launch_mlp_forward_tc_train(const void* mlp, const void* rows, const uint32_t* n_device, float* raw, uint32_t* error,
+                                        cudaStream_t s);
+// Backward of the MLPs over n rows (or *n_device when non-null): rows are
+// 64-byte feature rows with dirs (train_rows = 0) or the 112-byte training
+// rows of the forward (train_rows = 1, SH taken from the row); dout is the
+// loss-scaled d raw (n x 4).  Writes dfeat (n x 32 fp16) and one row of
+// kMlpParams weight gradients per CTA into partials; blocks is at most
+// mlp_backward_tc_blocks() (persistent CTAs, tile t to CTA t mod blocks).
+cudaError_t launch_mlp_backward_tc(const void* mlp, const void* rows, int train_rows, const float* dirs, const float* dout,
+                                   const uint32_t* n_device, uint32_t n, void* dfeat, float* partials, uint32_t blocks,
+                                   uint32_t* error, cudaStream_t s);
+uint32_t mlp_backward_tc_blocks();
+// Persistent grids of the forward / backward tensor-core MLP kernels and the
+// runtime's occupancy answer for each (CTAs per SM).
+void mlp_tc_info(uint32_t out[4]);
 
 // ---- sampler ----
 // Geometry of a marched training ray (48 bytes).

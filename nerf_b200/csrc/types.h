@@ -82,6 +82,7 @@ struct DeviceState {
     uint32_t counts_parity;  // which half of the per-ray count buffer the last step used
     unsigned long long total_samples;
     unsigned long long total_rays;
+    uint32_t mlp_error;   // a tensor-core MLP kernel's MMAs did not complete in time
 };
 
 // Data-parallel peer mode: synchronisation words of one rank, in its model

@@ -186,6 +186,73 @@ def test_mlp_only_matches_fused_field(cuda):
                                       part2_d.data_ptr(), mg2_d.data_ptr(), None) == abi.NERF_STATUS_INVALID_USAGE
 
 
+@pytest.mark.parametrize("n", [1, 127, 128, 3001])
+def test_mlp_forward_tc_matches_mma_sync(cuda, n):
+    """The tcgen05 MLP forward (128-row tiles, tensor-memory accumulators) against the mma.sync forward on the same
+    fp16 features and directions: the operands are rounded at the same points, only the fp32 accumulation order
+    differs, so raw outputs agree to well within the 1e-2 per-sample contract."""
+    torch = cuda
+    lib = abi.load()
+    rng = np.random.default_rng(21)
+    mlp = _mlp_params(rng).astype(np.float16).view(np.uint16)
+    feat = rng.standard_normal((n, 32)).astype(np.float16).view(np.uint16)
+    dirs = _unit_dirs(rng, n)
+    mlp_d, feat_d, dir_d = dev(torch, mlp), dev(torch, feat), dev(torch, dirs)
+    raw_d, raw_tc_d = zeros(torch, (n, 4), np.float32), zeros(torch, (n, 4), np.float32)
+    err_d = zeros(torch, 1, np.uint32)
+    check("mlp_forward", lib.nerf_b200_mlp_forward(mlp_d.data_ptr(), feat_d.data_ptr(), dir_d.data_ptr(), n, raw_d.data_ptr(), None))
+    check("mlp_forward_tc", lib.nerf_b200_mlp_forward_tc(mlp_d.data_ptr(), feat_d.data_ptr(), dir_d.data_ptr(), n,
+                                                         raw_tc_d.data_ptr(), err_d.data_ptr(), None))
+    torch.cuda.synchronize()
+    assert int(host(err_d)[0]) == 0
+    a, b = host(raw_d), host(raw_tc_d)
+    err = np.abs(a - b)
+    assert err.max() < 1e-2, err.max()
+    assert np.median(err) < 1e-3
+    want = oracle.mlp_forward(mlp, feat, dirs)
+    assert np.abs(b - want).max() < 1e-2
+
+
+@pytest.mark.parametrize("n", [1, 200, 3001])
+def test_mlp_backward_tc_matches_mma_sync(cuda, n):
+    """The tcgen05 MLP backward against the mma.sync backward on the same inputs: feature gradients within fp16
+    rounding of each other, weight gradients within 1e-2 relative L2 (fp32 accumulation in a different order),
+    and both against the CPU oracle."""
+    torch = cuda
+    lib = abi.load()
+    rng = np.random.default_rng(23)
+    mlp = _mlp_params(rng).astype(np.float16).view(np.uint16)
+    feat = rng.standard_normal((n, 32)).astype(np.float16).view(np.uint16)
+    dirs = _unit_dirs(rng, n)
+    dout = (rng.standard_normal((n, 4)) * 0.5).astype(np.float32)
+    mlp_d, feat_d, dir_d, dout_d = dev(torch, mlp), dev(torch, feat), dev(torch, dirs), dev(torch, dout)
+    parts = int(lib.nerf_b200_field_backward_partial_floats())
+    outs = []
+    for tc in (False, True):
+        dx_d, part_d, mg_d = zeros(torch, (n, 32), np.uint16), zeros(torch, parts, np.float32), zeros(torch, 10240, np.float32)
+        err_d = zeros(torch, 1, np.uint32)
+        if tc:
+            check("mlp_backward_tc", lib.nerf_b200_mlp_backward_tc(
+                mlp_d.data_ptr(), feat_d.data_ptr(), dir_d.data_ptr(), n, dout_d.data_ptr(), dx_d.data_ptr(),
+                part_d.data_ptr(), mg_d.data_ptr(), err_d.data_ptr(), None))
+        else:
+            check("mlp_backward", lib.nerf_b200_mlp_backward(
+                mlp_d.data_ptr(), feat_d.data_ptr(), dir_d.data_ptr(), n, dout_d.data_ptr(), dx_d.data_ptr(),
+                part_d.data_ptr(), mg_d.data_ptr(), None))
+        torch.cuda.synchronize()
+        assert int(host(err_d)[0]) == 0
+        outs.append((host(dx_d, np.uint16).view(np.float16).astype(np.float64), host(mg_d).astype(np.float64)))
+    (dx_ref, wg_ref), (dx_tc, wg_tc) = outs
+    assert np.abs(dx_tc - dx_ref).max() <= 5e-3 * max(1.0, np.abs(dx_ref).max())
+    assert np.linalg.norm(wg_tc - wg_ref) / np.linalg.norm(wg_ref) < 1e-2
+    for name, (a, b) in {"d0": (0, 2048), "d1": (2048, 3072), "c0": (3072, 5120), "c1": (5120, 9216), "c2": (9216, 9408)}.items():
+        assert np.linalg.norm(wg_tc[a:b] - wg_ref[a:b]) / (np.linalg.norm(wg_ref[a:b]) + 1e-30) < 1e-2, name
+    assert np.all(wg_tc[9408:] == 0)
+    dfeat_o, wg_o = oracle.mlp_backward(mlp, feat, dirs, dout)
+    assert np.linalg.norm(wg_tc - wg_o) / np.linalg.norm(wg_o) < 1e-2
+    assert np.linalg.norm(dx_tc - dfeat_o) / np.linalg.norm(dfeat_o) < 1e-2
+
+
 def _records(begin, count, gt, bg, dirs):
     n = len(begin)
     rec = np.zeros((n, 12), np.float32)

@@ -71,8 +71,10 @@ def test_initial_parameters_equal_oracle(cuda):
     ctx.close()
 
 
-@pytest.mark.parametrize("stop,background", [(0.0, 0), (1e-4, 1)])
-def test_first_step_matches_oracle(cuda, stop, background):
+@pytest.mark.parametrize("stop,background,mlp_tc", [(0.0, 0, "0"), (1e-4, 1, "0"), (0.0, 0, "1"), (1e-4, 1, "1")])
+def test_first_step_matches_oracle(cuda, monkeypatch, stop, background, mlp_tc):
+    """mlp_tc "1": the training step's MLPs on tcgen05 (encode kernel + tensor-core MLP kernels)."""
+    monkeypatch.setenv("NERF_B200_MLP_TC", mlp_tc)
     _, ctx, oc, cfg = make_pair(stop=stop, background=background)
     ctx.train_step()
     oc.step()
@@ -95,7 +97,9 @@ def test_first_step_matches_oracle(cuda, stop, background):
     ctx.close()
 
 
-def test_warmup_steps_sampler_bit_exact(cuda):
+@pytest.mark.parametrize("mlp_tc", ["0", "1"])
+def test_warmup_steps_sampler_bit_exact(cuda, monkeypatch, mlp_tc):
+    monkeypatch.setenv("NERF_B200_MLP_TC", mlp_tc)
     _, ctx, oc, _ = make_pair(warmup=6, interval=2)
     losses = []
     for step in range(5):
