@@ -695,7 +695,8 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = launch_grad_stats(op, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     // The statistics kernel advanced the frame and set the next ray count:
     // the next step's march.  (Run beside Adam on a second stream it gained
-    // nothing: the concurrent blocks slowed Adam down by the march's time.)
+    // nothing: with HBM saturated by Adam the march's stores stall, and the
+    // pair took longer than the two in order.)
     if ((e = launch_march(sa, s)) != cudaSuccess || (e = launch_adam(op, s)) != cudaSuccess) return e;
     // Peer mode: every rank wrote its owned fp16 parameters into every rank's
     // mirror; no rank reads them before all writes are done.
@@ -1259,7 +1260,11 @@ NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out
     // occupancy query + update, sampler (3), forward, composite, backward MLP +
     // scatter, statistics, march, Adam; data-parallel: + weight-gradient
     // reduce, and in peer mode 3 barriers + the gradient reduction.
-    out->kernels_per_step = 12u + (c->comm ? 1u : 0u) + (c->dp_peer ? 4u : 0u);
+    // occupancy query + update, march, 3 sampler kernels, forward, composite,
+    // MLP backward + scatter, statistics, Adam (the tensor-core path splits the
+    // forward into encode + MLP); data parallel adds the weight-gradient
+    // reduction, and peer mode its barriers and gradient reduction.
+    out->kernels_per_step = 12u + (c->mlp_tc ? 1u : 0u) + (c->comm ? 1u : 0u) + (c->dp_peer ? 4u : 0u);
     out->dp_peer = c->dp_peer ? 1u : 0u;
     return NERF_STATUS_OK;
 }
