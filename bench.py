@@ -230,6 +230,8 @@ def run_ours(args):
     kernels = kernel_table(ctx, prof, mean_samples)
     l2 = l2_peaks(lib, stream)
     for k in kernels:  # L2-bound field kernels against the measured L2 peaks
+        if k["ms"] <= 0.0:
+            continue
         if k["kernel"] == "field_forward":
             k["l2_gather_gbs"] = mean_samples * 128 * 4 / (k["ms"] / 1e3) / 1e9
             k["l2_frac"] = k["l2_gather_gbs"] / l2["read_gbs"]
