@@ -103,6 +103,18 @@ NERF_API NerfStatus nerf_b200_param_counts(void* context, uint64_t* n_grid, uint
 /* Host buffers of n_grid + n_mlp elements; NULL skips. */
 NERF_API NerfStatus nerf_b200_read_params(void* context, float* master, uint16_t* params_f16, float* adam_m, float* adam_v);
 NERF_API NerfStatus nerf_b200_write_params(void* context, const float* master);
+/* Training-state checkpoint for an exact resume (extends the reference's
+ * weights-only nerf_save_network_weights, backend-cuda.cu:2466-2592, whose
+ * load resets the optimiser and occupancy): fp32 masters, both Adam moments,
+ * occupancy densities and bitfield, and the step state (frame, next ray
+ * count, counters, last statistics), in the same container (u64 header
+ * length, JSON header, raw tensors).  Both need a configured context
+ * (NERF_STATUS_STATE_ERROR otherwise); load fails with NERF_STATUS_IO_ERROR
+ * when the file is missing, malformed, or sized for another hash grid or
+ * occupancy grid.  After a load the next nerf_train_step samples exactly the
+ * rays the saved run would have sampled. */
+NERF_API NerfStatus nerf_b200_save_training_state(void* context, const char* path_utf8);
+NERF_API NerfStatus nerf_b200_load_training_state(void* context, const char* path_utf8);
 /* density: grid_res^3 floats; bitfield: ceil(grid_res^3/32) words; NULL skips. */
 NERF_API NerfStatus nerf_b200_read_occupancy(void* context, float* density, uint32_t* bitfield);
 NERF_API NerfStatus nerf_b200_write_occupancy(void* context, const float* density, const uint32_t* bitfield);

@@ -164,6 +164,13 @@ class Context:
         check("nerf_load_network_weights", self.lib.nerf_load_network_weights(self.handle, C.byref(d)))
 
     # ---- nerf_b200.h
+    def save_state(self, path: str):
+        """Training-state checkpoint (masters, Adam moments, occupancy, step state) for an exact resume."""
+        check("nerf_b200_save_training_state", lib().nerf_b200_save_training_state(self.handle, str(path).encode()))
+
+    def load_state(self, path: str):
+        check("nerf_b200_load_training_state", lib().nerf_b200_load_training_state(self.handle, str(path).encode()))
+
     def counters(self) -> NerfB200Counters:
         c = NerfB200Counters()
         check("nerf_b200_read_counters", self.lib.nerf_b200_read_counters(self.handle, C.byref(c)))

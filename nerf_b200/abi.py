@@ -283,6 +283,8 @@ B200_EXPORTS = {
     "nerf_b200_mlp_forward_tc": (S, [P, P, P, U32, P, P, P]),
     "nerf_b200_mlp_backward_tc": (S, [P, P, P, U32, P, P, P, P, P, P]),
     "nerf_b200_mlp_tc_info": (S, [P]),
+    "nerf_b200_save_training_state": (S, [P, C.c_char_p]),
+    "nerf_b200_load_training_state": (S, [P, C.c_char_p]),
     "nerf_b200_field_backward_noalloc_max_rows": (U32, []),
     "nerf_b200_field_backward_noalloc": (S, [C.POINTER(NerfB200GridLayout), P, P, P, U32, P, P, P, P, P]),
     "nerf_b200_probe_l2_read": (S, [P, C.c_uint64, U32, P, P]),

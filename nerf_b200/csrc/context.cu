@@ -1241,6 +1241,127 @@ NERF_API NerfStatus nerf_load_network_weights(void* context, const NerfCheckpoin
     return NERF_STATUS_OK;
 }
 
+// Training-state checkpoint: the same container (u64 header length, JSON
+// header, raw tensors) with every tensor a training step reads besides the
+// dataset: fp32 masters, both Adam moments, the occupancy densities and
+// bitfield, and the step state (frame, ray count, counters, last statistics).
+namespace {
+struct StateBlob {
+    const char* name;
+    const char* dtype;
+    uint64_t count, elem;
+    void* host;
+};
+std::vector<StateBlob> state_blobs(Context* c, std::vector<float>& master, std::vector<float>& am, std::vector<float>& av,
+                                   std::vector<float>& density, std::vector<uint32_t>& bits, nb::DeviceState& st) {
+    master.resize(c->n_params);
+    am.resize(c->n_params);
+    av.resize(c->n_params);
+    density.resize(c->cell_count);
+    bits.resize(c->words);
+    return {{"params.master", "F32", c->n_params, 4u, master.data()},
+            {"adam.m", "F32", c->n_params, 4u, am.data()},
+            {"adam.v", "F32", c->n_params, 4u, av.data()},
+            {"occupancy.density", "F32", c->cell_count, 4u, density.data()},
+            {"occupancy.bitfield", "U32", c->words, 4u, bits.data()},
+            {"step.state", "U8", sizeof(nb::DeviceState), 1u, &st}};
+}
+}  // namespace
+
+NERF_API NerfStatus nerf_b200_save_training_state(void* context, const char* path_utf8) {
+    if (!context || !path_utf8) return NERF_STATUS_INVALID_USAGE;
+    Context* c = as_ctx(context);
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (!c->configured) return NERF_STATUS_STATE_ERROR;
+    std::vector<float> master, am, av, density;
+    std::vector<uint32_t> bits;
+    nb::DeviceState st{};
+    const auto blobs = state_blobs(c, master, am, av, density, bits, st);
+    NB_TRY(cudaStreamSynchronize(c->stream));
+    NB_TRY(c->read_sharded(master.data(), c->master, c->n_params));
+    NB_TRY(c->read_sharded(am.data(), c->m, c->n_params));
+    NB_TRY(c->read_sharded(av.data(), c->v, c->n_params));
+    NB_TRY(cudaMemcpy(density.data(), c->density, c->cell_count * 4ull, cudaMemcpyDeviceToHost));
+    NB_TRY(cudaMemcpy(bits.data(), c->bitfield, c->words * 4ull, cudaMemcpyDeviceToHost));
+    NB_TRY(cudaMemcpy(&st, c->state, sizeof(st), cudaMemcpyDeviceToHost));
+    char buf[512];
+    std::snprintf(buf, sizeof(buf),
+                  "{\"__metadata__\":{\"format\":\"nerf-b200/training-state-v1\",\"log2_hashmap_size\":%u,"
+                  "\"base_resolution\":%u,\"max_resolution\":%u,\"occupancy_grid_res\":%u,\"frame_index\":%u}",
+                  c->grid.log2_hashmap_size, c->grid.base_resolution, c->grid.max_resolution, c->grid_res, st.frame_index);
+    std::string h = buf;
+    uint64_t off = 0;
+    for (const auto& b : blobs) {
+        std::snprintf(buf, sizeof(buf), ",\"%s\":{\"dtype\":\"%s\",\"shape\":[%llu],\"data_offsets\":[%llu,%llu]}", b.name,
+                      b.dtype, static_cast<unsigned long long>(b.count), static_cast<unsigned long long>(off),
+                      static_cast<unsigned long long>(off + b.count * b.elem));
+        h += buf;
+        off += b.count * b.elem;
+    }
+    h += "}";
+    std::ofstream f(path_utf8, std::ios::binary | std::ios::trunc);
+    if (!f) return NERF_STATUS_IO_ERROR;
+    const uint64_t len = h.size();
+    f.write(reinterpret_cast<const char*>(&len), 8);
+    f.write(h.data(), static_cast<std::streamsize>(h.size()));
+    for (const auto& b : blobs) f.write(static_cast<const char*>(b.host), static_cast<std::streamsize>(b.count * b.elem));
+    return f.good() ? NERF_STATUS_OK : NERF_STATUS_IO_ERROR;
+}
+
+NERF_API NerfStatus nerf_b200_load_training_state(void* context, const char* path_utf8) {
+    if (!context || !path_utf8) return NERF_STATUS_INVALID_USAGE;
+    Context* c = as_ctx(context);
+    if (!c->configured) return NERF_STATUS_STATE_ERROR;
+    std::vector<float> master, am, av, density;
+    std::vector<uint32_t> bits;
+    nb::DeviceState st{};
+    const auto blobs = state_blobs(c, master, am, av, density, bits, st);
+    try {
+        std::ifstream f(path_utf8, std::ios::binary);
+        if (!f) return NERF_STATUS_IO_ERROR;
+        uint64_t len = 0;
+        f.read(reinterpret_cast<char*>(&len), 8);
+        if (!f || len == 0u || len > (64ull << 20)) return NERF_STATUS_IO_ERROR;
+        std::string header(len, '\0');
+        f.read(header.data(), static_cast<std::streamsize>(len));
+        if (!f) return NERF_STATUS_IO_ERROR;
+        std::map<std::string, nb::ckpt::Entry> entries;
+        if (!nb::ckpt::parse(header, entries)) return NERF_STATUS_IO_ERROR;
+        for (const auto& b : blobs) {  // every tensor present with this context's size
+            auto it = entries.find(b.name);
+            if (it == entries.end()) return NERF_STATUS_IO_ERROR;
+            const auto& e = it->second;
+            if (e.shape.size() != 1 || e.shape[0] != b.count || e.offsets.size() != 2 || e.offsets[1] - e.offsets[0] != b.count * b.elem)
+                return NERF_STATUS_IO_ERROR;
+            f.seekg(static_cast<std::streamoff>(8u + len + e.offsets[0]), std::ios::beg);
+            f.read(static_cast<char*>(b.host), static_cast<std::streamsize>(b.count * b.elem));
+            if (!f) return NERF_STATUS_IO_ERROR;
+        }
+    } catch (...) {
+        return NERF_STATUS_IO_ERROR;
+    }
+    std::lock_guard<std::mutex> lk(c->mu);
+    NB_TRY(cudaStreamSynchronize(c->stream));
+    // Every rank writes the whole vectors (peer mode reads only its owned range).
+    NB_TRY(cudaMemcpy(c->master, master.data(), c->n_params * 4, cudaMemcpyHostToDevice));
+    NB_TRY(cudaMemcpy(c->m, am.data(), c->n_params * 4, cudaMemcpyHostToDevice));
+    NB_TRY(cudaMemcpy(c->v, av.data(), c->n_params * 4, cudaMemcpyHostToDevice));
+    NB_TRY(nb::launch_f32_to_f16(c->master, c->p16, c->n_params, c->stream));  // the fp16 mirror is rn(master)
+    NB_TRY(cudaMemsetAsync(c->grid_grad, 0, c->n_grid * 2, c->stream));
+    NB_TRY(cudaMemsetAsync(c->mlp_grad, 0, nb::kMlpGradSlots * 4, c->stream));
+    NB_TRY(cudaMemcpyAsync(c->density, density.data(), c->cell_count * 4ull, cudaMemcpyHostToDevice, c->stream));
+    NB_TRY(cudaMemcpyAsync(c->bitfield, bits.data(), c->words * 4ull, cudaMemcpyHostToDevice, c->stream));
+    st.done_blocks = 0u;
+    st.grad_sumsq = 0.0f;
+    st.nonfinite = 0u;
+    NB_TRY(cudaMemcpyAsync(c->state, &st, sizeof(st), cudaMemcpyHostToDevice, c->stream));
+    NB_TRY(nb::launch_march(c->sampler_args(), c->stream));  // the next step's march (frame and ray count restored)
+    NB_TRY(cudaStreamSynchronize(c->stream));
+    c->occupancy_valid = true;
+    c->host_generation = st.frame_index;
+    return NERF_STATUS_OK;
+}
+
 // ============================================================= nerf_b200.h
 NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out) {
     if (!context || !out) return NERF_STATUS_INVALID_USAGE;

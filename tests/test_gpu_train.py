@@ -263,6 +263,65 @@ def test_checkpoint_roundtrip_and_reset(cuda):
     ctx.close()
 
 
+def _snapshot(ctx):
+    master, p16, m, v = ctx.params()
+    d, b = ctx.occupancy()
+    c = ctx.counters()
+    return master, p16, m, v, d, b, (c.frame_index, c.next_rays, c.total_samples, c.total_rays, c.samples)
+
+
+def test_training_state_resume(cuda):
+    """Exact resume: a fresh context that loads the training state holds the saved masters, fp16 mirror, Adam moments,
+    occupancy and step state bit for bit, and its next steps sample exactly the rays of the uninterrupted run (the
+    sampler, the occupancy refresh and the step counters are deterministic); parameters after the resumed steps agree
+    within the run-to-run spread of the fp16 gradient reductions."""
+    # refresh at frames 4 and 8: the saved state holds a refreshed grid, and the three resumed steps (frames 5-7)
+    # sample from it alone
+    _, ctx, _, _ = make_pair(warmup=2, interval=4, target=3000, max_samples=8192)
+    for _ in range(5):
+        ctx.train_step()
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "state.nerf")
+        ctx.save_state(path)
+        saved = _snapshot(ctx)
+        batches = []
+        for _ in range(3):
+            ctx.train_step()
+            batches.append(ctx.batch())
+        after = ctx.params()[0]
+        _, ctx2, _, _ = make_pair(warmup=2, interval=4, target=3000, max_samples=8192)
+        ctx2.load_state(path)
+        restored = _snapshot(ctx2)
+        for a, b in zip(saved[:6], restored[:6]):
+            assert np.array_equal(np.asarray(a).view(np.uint8), np.asarray(b).view(np.uint8))
+        assert saved[6] == restored[6]
+        for want in batches:
+            ctx2.train_step()
+            got = ctx2.batch()
+            for k in ("counts", "index", "begin", "count"):
+                assert np.array_equal(got[k], want[k]), k
+            assert np.array_equal(got["pos_dt"].view(np.uint32), want["pos_dt"].view(np.uint32))
+        after2 = ctx2.params()[0]
+        assert np.linalg.norm(after2 - after) <= 1e-3 * np.linalg.norm(after)
+        # a state for another hash-grid size is refused; so are missing and unconfigured cases
+        ds = nerf_b200.make_scene(kind=0, seed=0, n_views=2, width=16, height=16)
+        other = nerf_b200.Context(ds, grid_res=RES, max_sample_steps=RAYS * STEPS, max_batch_rays=4 * RAYS,
+                                  options=nerf_b200.default_options(log2_hashmap_size=14, max_resolution=512))
+        with pytest.raises(abi.NerfError) as e:
+            other.load_state(path)
+        assert e.value.status == abi.NERF_STATUS_STATE_ERROR
+        other.configure(nerf_b200.training_config(rays=RAYS, steps=STEPS))
+        with pytest.raises(abi.NerfError) as e:
+            other.load_state(path)
+        assert e.value.status == abi.NERF_STATUS_IO_ERROR
+        with pytest.raises(abi.NerfError) as e:
+            ctx2.load_state(os.path.join(td, "missing.nerf"))
+        assert e.value.status == abi.NERF_STATUS_IO_ERROR
+        other.close()
+        ctx2.close()
+    ctx.close()
+
+
 def test_error_codes(cuda):
     ds = nerf_b200.make_scene(n_views=4, width=16, height=16)
     ctx = nerf_b200.Context(ds, grid_res=16, max_sample_steps=1 << 16, max_batch_rays=256)
