@@ -253,6 +253,9 @@ def run_ours(args):
     cpu = None
     if rank == 0 and not args.skip_cpu:
         cpu = cpu_baseline(nb, ds, args)
+    dio = None
+    if rank == 0 and not args.skip_dataset_io:
+        dio = dataset_io(lib, ds)
 
     if rank == 0:
         hbm, src = peaks()
@@ -275,6 +278,7 @@ def run_ours(args):
             "render": render,
             "psnr": psnr,
             "cpu_baseline": cpu,
+            "dataset_io": dio,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -477,6 +481,46 @@ def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
             "h2d_bytes_per_step": h2d / steps, "d2h_bytes_per_step": 20,
             "note": "create+upload, configure and every step train_step + read_train_stats, wall clock, max over ranks; "
                     "includes the occupancy warm-up phase of a fresh job"}
+
+
+def dataset_io(lib, ds):
+    """The config-2 dataset through the reference's file format (Blender transforms JSON + RGBA8 PNG): written once,
+    then loaded into pinned host memory with all host threads and with one (the reference driver decodes its PNGs one
+    after another with stb_image, benchmark.cpp:188-205)."""
+    import ctypes as C
+    import shutil
+    import tempfile
+
+    import torch
+    from nerf_b200 import abi
+    n, h, w = ds.images.shape[:3]
+    d = tempfile.mkdtemp(prefix="nerf_b200_ds_")
+    try:
+        imgs = np.ascontiguousarray(ds.images)
+        cams = np.ascontiguousarray(ds.cameras)
+        t0 = time.perf_counter()
+        abi.check("blender write", lib.nerf_b200_blender_write(d.encode(), imgs.ctypes.data, cams.ctypes.data, n, w, h,
+                                                              CFG2["fov"], 0))
+        t_write = time.perf_counter() - t0
+        dst = torch.empty(imgs.nbytes, dtype=torch.uint8)
+        if torch.cuda.is_available():
+            dst = dst.pin_memory()
+        cam_out = np.zeros((n, 4, 4), np.float32)
+        intr = np.zeros(4, np.float32)
+        res = {"images": n, "resolution": f"{w}x{h}", "bytes_rgba8": int(imgs.nbytes), "write_s": t_write}
+        for threads, key in ((0, "load_all_threads"), (1, "load_one_thread")):
+            t0 = time.perf_counter()
+            abi.check("blender load", lib.nerf_b200_blender_load(d.encode(), 0, threads, dst.data_ptr(), imgs.nbytes,
+                                                                cam_out.ctypes.data, intr.ctypes.data))
+            dt = time.perf_counter() - t0
+            res[key] = {"s": dt, "images_per_s": n / dt, "MB_per_s": imgs.nbytes / dt / 1e6}
+        res["bit_exact"] = bool(np.array_equal(dst.numpy().reshape(imgs.shape), imgs))
+        res["threads"] = os.cpu_count()
+        res["note"] = ("PNG stored-deflate files written by nerf_b200_blender_write, decoded by nerf_b200_blender_load "
+                       "(inflate, CRC-32 / Adler-32 checks, unfilter) into pinned memory; host wall clock")
+        return res
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
 
 
 def cpu_baseline(nb, ds, args, steps=None, threads=None, seconds=20.0):
@@ -729,6 +773,7 @@ def main():
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-reference-cuda", action="store_true")
+    ap.add_argument("--skip-dataset-io", action="store_true")
     ap.add_argument("--micro", action="store_true", help="kernel microbench sweep (config 5) instead of the step")
     ap.add_argument("--micro-reps", type=int, default=10)
     ap.add_argument("--micro-points", type=int, nargs="*", default=[20, 22, 24])

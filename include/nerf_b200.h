@@ -201,6 +201,39 @@ typedef struct NerfB200SceneDesc {
 NERF_API NerfStatus nerf_b200_scene_render(const NerfB200SceneDesc* desc, uint8_t* images_rgba8, float* cameras_4x4,
                                            float* intrinsics4);
 
+/* ------------------------------------------------------------ datasets */
+/* The reference's dataset format (its driver's loader, benchmark.cpp:148-303):
+ * a Blender "transforms" JSON (camera_angle_x; frames with file_path and a
+ * row-major 4x4 transform_matrix) next to 8-bit PNG images.  path is the JSON
+ * file or its directory (then transforms_train.json); a file_path without an
+ * extension gets ".png".  PNG: 8-bit grey, grey + alpha, RGB, RGBA or palette,
+ * not interlaced, decoded to RGBA8.  Errors: NERF_STATUS_IO_ERROR for missing or
+ * malformed files, NERF_STATUS_INVALID_USAGE for null arguments, a buffer too
+ * small, or images of different sizes.  No counterpart in the reference
+ * library: its driver does this with nlohmann::json and stb_image. */
+typedef struct NerfB200BlenderInfo {
+    uint32_t image_count;
+    uint32_t width;
+    uint32_t height;
+    float camera_angle_x;
+} NerfB200BlenderInfo;
+NERF_API NerfStatus nerf_b200_blender_probe(const char* path, NerfB200BlenderInfo* out);
+/* Decodes every image on n_threads threads (0: all host threads) into
+ * images_rgba8 ([n][H][W][4], e.g. pinned memory for nerf_create_context) and
+ * writes the cameras and (fx, fy, cx, cy) = ((W/2) / tan(angle/2), same,
+ * (W-1)/2, (H-1)/2).  remap = 1 applies the reference driver's convention
+ * (world axes (x, -z, y) -> (x, y, z), translation * 0.33 + 0.5: the scene in
+ * [0,1]^3); remap = 0 keeps the file's matrices. */
+NERF_API NerfStatus nerf_b200_blender_load(const char* path, uint32_t remap, uint32_t n_threads, uint8_t* images_rgba8,
+                                           uint64_t images_bytes, float* cameras_4x4, float* intrinsics4);
+/* Writes dir/transforms_train.json and dir/train/r_<i>.png (RGBA8). */
+NERF_API NerfStatus nerf_b200_blender_write(const char* dir, const uint8_t* images_rgba8, const float* cameras_4x4, uint32_t n,
+                                            uint32_t width, uint32_t height, float camera_angle_x, uint32_t n_threads);
+/* One PNG: read into rgba8 (bytes capacity; NULL rgba8 only reports the size),
+ * or write RGBA8 (filter 0, deflate stored blocks). */
+NERF_API NerfStatus nerf_b200_png_read(const char* path, uint8_t* rgba8, uint64_t bytes, uint32_t* width, uint32_t* height);
+NERF_API NerfStatus nerf_b200_png_write(const char* path, const uint8_t* rgba8, uint32_t width, uint32_t height);
+
 /* ------------------------------------- kernel-level entry points (tests) */
 /* All pointers are device pointers; stream is a cudaStream_t (NULL = legacy
  * default stream).  Calls are asynchronous. */

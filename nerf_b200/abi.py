@@ -242,6 +242,11 @@ U64 = C.c_uint64
 F32 = C.c_float
 S = C.c_int  # NerfStatus
 
+
+class NerfB200BlenderInfo(C.Structure):
+    _fields_ = [("image_count", C.c_uint32), ("width", C.c_uint32), ("height", C.c_uint32), ("camera_angle_x", C.c_float)]
+
+
 # name -> (restype, argtypes); the ABI surface, in header order.
 NERF_H_EXPORTS = {
     "nerf_create_context": (S, [C.POINTER(NerfCreateDesc), C.POINTER(P)]),
@@ -284,6 +289,11 @@ B200_EXPORTS = {
     "nerf_b200_mlp_backward_tc": (S, [P, P, P, U32, P, P, P, P, P, P]),
     "nerf_b200_mlp_tc_info": (S, [P]),
     "nerf_b200_save_training_state": (S, [P, C.c_char_p]),
+    "nerf_b200_blender_probe": (S, [C.c_char_p, P]),
+    "nerf_b200_blender_load": (S, [C.c_char_p, U32, U32, P, U64, P, P]),
+    "nerf_b200_blender_write": (S, [C.c_char_p, P, P, U32, U32, U32, F32, U32]),
+    "nerf_b200_png_read": (S, [C.c_char_p, P, U64, P, P]),
+    "nerf_b200_png_write": (S, [C.c_char_p, P, U32, U32]),
     "nerf_b200_load_training_state": (S, [P, C.c_char_p]),
     "nerf_b200_field_backward_noalloc_max_rows": (U32, []),
     "nerf_b200_field_backward_noalloc": (S, [C.POINTER(NerfB200GridLayout), P, P, P, U32, P, P, P, P, P]),
