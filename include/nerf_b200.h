@@ -39,11 +39,15 @@ typedef struct NerfB200Options {
     float render_stop_transmittance;  /* nerf_inference: same for rendering              */
     uint32_t target_samples_per_step; /* 0: fixed rays_per_batch; else adapt ray count   */
     uint32_t max_samples_per_step;    /* 0: rays_per_batch * max_sample_steps_per_ray    */
+    uint32_t n_cascades;              /* occupancy cascades (1..8): cascade k covers the
+                                         configured AABB scaled by 2^k about its centre,
+                                         each with grid_res^3 cells; rays march the
+                                         outermost box, positions are normalised in it */
 } NerfB200Options;
 
 /* Defaults, then overrides from NERF_B200_* environment variables
  * (LOG2_HASHMAP_SIZE, BASE_RESOLUTION, MAX_RESOLUTION, BACKGROUND, STOP_T,
- * RENDER_STOP_T, TARGET_SAMPLES, MAX_SAMPLES). */
+ * RENDER_STOP_T, TARGET_SAMPLES, MAX_SAMPLES, CASCADES). */
 NERF_API void nerf_b200_default_options(NerfB200Options* out);
 /* nerf_create_context with explicit options (nerf_create_context uses the defaults). */
 NERF_API NerfStatus nerf_b200_create_context(const NerfCreateDesc* desc, const NerfB200Options* options, void** out_context);
@@ -115,7 +119,7 @@ NERF_API NerfStatus nerf_b200_write_params(void* context, const float* master);
  * rays the saved run would have sampled. */
 NERF_API NerfStatus nerf_b200_save_training_state(void* context, const char* path_utf8);
 NERF_API NerfStatus nerf_b200_load_training_state(void* context, const char* path_utf8);
-/* density: grid_res^3 floats; bitfield: ceil(grid_res^3/32) words; NULL skips. */
+/* density: n_cascades * grid_res^3 floats; bitfield: ceil(that / 32) words; NULL skips. */
 NERF_API NerfStatus nerf_b200_read_occupancy(void* context, float* density, uint32_t* bitfield);
 NERF_API NerfStatus nerf_b200_write_occupancy(void* context, const float* density, const uint32_t* bitfield);
 NERF_API NerfStatus nerf_b200_set_frame_index(void* context, uint32_t frame_index);

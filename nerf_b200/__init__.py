@@ -111,6 +111,7 @@ class Context:
         self.grid_res = grid_res
         self.handle = C.c_void_p()
         opts = options if options is not None else default_options()
+        self.cascades = max(1, int(opts.n_cascades))
         check("nerf_b200_create_context",
               self.lib.nerf_b200_create_context(C.byref(self.desc), C.byref(opts), C.byref(self.handle)))
         n_grid, n_mlp = C.c_uint64(), C.c_uint64()
@@ -194,7 +195,7 @@ class Context:
         check("nerf_b200_write_params", self.lib.nerf_b200_write_params(self.handle, _ptr(master)))
 
     def occupancy(self):
-        cells = self.grid_res ** 3
+        cells = self.grid_res ** 3 * self.cascades
         dens = np.zeros(cells, np.float32)
         bits = np.zeros((cells + 31) // 32, np.uint32)
         check("nerf_b200_read_occupancy", self.lib.nerf_b200_read_occupancy(self.handle, _ptr(dens), _ptr(bits)))

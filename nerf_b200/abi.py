@@ -138,6 +138,7 @@ class NerfB200Options(C.Structure):
         ("render_stop_transmittance", C.c_float),
         ("target_samples_per_step", C.c_uint32),
         ("max_samples_per_step", C.c_uint32),
+        ("n_cascades", C.c_uint32),
     ]
 
 

@@ -303,7 +303,9 @@ struct Context {
                            NerfB200RenderInfo* info);
     FieldArgs field_args() const;
     SamplerArgs sampler_args() const;
-    void fill_aabb(float* mn, float* mx, float* size) const;
+    void fill_aabb(float* mn, float* mx, float* size, const NerfTrainingConfig* with = nullptr) const;
+    void base_aabb(float* mn, float* mx, const NerfTrainingConfig* with = nullptr) const;
+    CascadeBox cascade_box(const NerfTrainingConfig* with = nullptr) const;
 };
 
 FieldArgs Context::field_args() const {
@@ -313,20 +315,55 @@ FieldArgs Context::field_args() const {
     a.mlp_offset = static_cast<uint32_t>(n_grid);
     a.state = state;
     fill_aabb(a.aabb_min, a.aabb_max, a.aabb_size);
+    a.casc = cascade_box();
     return a;
 }
 
-void Context::fill_aabb(float* mn, float* mx, float* size) const {
-    if (configured) {
-        mn[0] = cfg.aabb_min_x;
-        mn[1] = cfg.aabb_min_y;
-        mn[2] = cfg.aabb_min_z;
-        mx[0] = cfg.aabb_max_x;
-        mx[1] = cfg.aabb_max_y;
-        mx[2] = cfg.aabb_max_z;
-    } else {  // the reference renders [0,1]^3 before configuration
+// The configured AABB (cascade 0), or [0,1]^3 before configuration (the
+// reference renders that box then).  During configure the new configuration
+// is passed explicitly.
+void Context::base_aabb(float* mn, float* mx, const NerfTrainingConfig* with) const {
+    const NerfTrainingConfig* c = with ? with : (configured ? &cfg : nullptr);
+    if (c) {
+        mn[0] = c->aabb_min_x;
+        mn[1] = c->aabb_min_y;
+        mn[2] = c->aabb_min_z;
+        mx[0] = c->aabb_max_x;
+        mx[1] = c->aabb_max_y;
+        mx[2] = c->aabb_max_z;
+    } else {
         mn[0] = mn[1] = mn[2] = 0.0f;
         mx[0] = mx[1] = mx[2] = 1.0f;
+    }
+}
+
+// Cascade k covers centre +- half * 2^k, centre = (min + max) / 2,
+// half = size / 2 (exact).
+CascadeBox Context::cascade_box(const NerfTrainingConfig* with) const {
+    CascadeBox b{};
+    float mn[3], mx[3];
+    base_aabb(mn, mx, with);
+    for (int k = 0; k < 3; ++k) {
+        b.bmn[k] = mn[k];
+        b.bsize[k] = mx[k] - mn[k];
+        b.c[k] = (mn[k] + mx[k]) * 0.5f;
+        b.h[k] = b.bsize[k] * 0.5f;
+    }
+    b.cascades = opt.n_cascades;
+    return b;
+}
+
+// Marching box: the outermost cascade (the configured AABB with one cascade).
+void Context::fill_aabb(float* mn, float* mx, float* size, const NerfTrainingConfig* with) const {
+    base_aabb(mn, mx, with);
+    if (opt.n_cascades > 1u) {
+        const CascadeBox b = cascade_box(with);
+        const float s = std::ldexp(1.0f, static_cast<int>(opt.n_cascades) - 1);
+        for (int k = 0; k < 3; ++k) {
+            const float hs = b.h[k] * s;
+            mn[k] = b.c[k] - hs;
+            mx[k] = b.c[k] + hs;
+        }
     }
     for (int k = 0; k < 3; ++k) size[k] = mx[k] - mn[k];
 }
@@ -334,6 +371,7 @@ void Context::fill_aabb(float* mn, float* mx, float* size) const {
 NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     opt = o;
     if (opt.n_levels != 16u) return NERF_STATUS_INVALID_USAGE;  // the fused field takes 16 levels x 2 features
+    if (opt.n_cascades == 0u || opt.n_cascades > 8u) return NERF_STATUS_INVALID_USAGE;
     if (grid_layout(opt.n_levels, opt.log2_hashmap_size, opt.base_resolution, opt.max_resolution, &grid) != 0)
         return NERF_STATUS_INVALID_USAGE;
     lt = make_level_table(grid);
@@ -347,7 +385,7 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     cx = d.cx;
     cy = d.cy;
     grid_res = d.occupancy_grid_res;
-    cell_count = grid_res * grid_res * grid_res;
+    cell_count = grid_res * grid_res * grid_res * opt.n_cascades;  // cascade after cascade
     words = (cell_count + 31u) / 32u;
     max_sample_steps = d.max_sample_steps;
     max_batch_rays = d.max_batch_rays;
@@ -461,12 +499,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     t.fy = fy;
     t.cx = cx;
     t.cy = cy;
-    const float mn[3] = {c.aabb_min_x, c.aabb_min_y, c.aabb_min_z}, mx[3] = {c.aabb_max_x, c.aabb_max_y, c.aabb_max_z};
-    for (int k = 0; k < 3; ++k) {
-        t.aabb_min[k] = mn[k];
-        t.aabb_max[k] = mx[k];
-        t.aabb_size[k] = mx[k] - mn[k];
-    }
+    fill_aabb(t.aabb_min, t.aabb_max, t.aabb_size, &c);  // the new configuration's box (outermost cascade)
+    t.casc = cascade_box(&c);
     const float ifx = fx > 0.0f ? 1.0f / fx : 0.0f, ify = fy > 0.0f ? 1.0f / fy : 0.0f;
     t.cone = 0.5f * (ifx + ify);
     t.max_rays = max_batch_rays;
@@ -831,6 +865,7 @@ NerfStatus Context::render_view(const float* c2w, uint32_t w, uint32_t h, float 
     ra.bitfield = occupancy_valid ? bitfield : full_bitfield;
     ra.grid_res = grid_res;
     fill_aabb(ra.aabb_min, ra.aabb_max, ra.aabb_size);
+    ra.casc = cascade_box();
     std::memcpy(ra.c2w, c2w, 12 * sizeof(float));
     ra.width = w;
     ra.height = h;
@@ -1042,6 +1077,7 @@ NERF_API void nerf_b200_default_options(NerfB200Options* o) {
     o->render_stop_transmittance = nb::env_float("NERF_B200_RENDER_STOP_T", 1e-4f);
     o->target_samples_per_step = nb::env_u32("NERF_B200_TARGET_SAMPLES", 0u);
     o->max_samples_per_step = nb::env_u32("NERF_B200_MAX_SAMPLES", 0u);
+    o->n_cascades = nb::env_u32("NERF_B200_CASCADES", 1u);
 }
 
 NERF_API NerfStatus nerf_b200_create_context(const NerfCreateDesc* desc, const NerfB200Options* options, void** out) {

@@ -297,17 +297,22 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
             d[1] = ray.dir[1];
             d[2] = ray.dir[2];
         } else if (mode == kFieldOccupancy) {
-            const uint32_t R = a.grid_res;
+            // Cell (cascade after cascade, x fastest) of the round-robin window;
+            // its centre in its cascade's box.
+            const uint32_t R = a.grid_res, RRR = R * R * R;
             const uint32_t start =
                 static_cast<uint32_t>(static_cast<unsigned long long>(a.state->frame_index) * a.update_count % a.cell_count);
-            const uint32_t cell = static_cast<uint32_t>((static_cast<unsigned long long>(start) + r) % a.cell_count);
+            const uint32_t q = static_cast<uint32_t>((static_cast<unsigned long long>(start) + r) % a.cell_count);
+            const uint32_t mip = q / RRR, cell = q - mip * RRR;
             const uint32_t z = cell / (R * R), rem = cell - z * R * R, y = rem / R, x = rem - y * R;
             const uint32_t ci[3] = {x, y, z};
+            const float s = pow2f(mip);
             float c[3];
 #pragma unroll
             for (int k = 0; k < 3; ++k) {
-                const float step = __fdiv_rn(__fsub_rn(a.aabb_max[k], a.aabb_min[k]), static_cast<float>(R));
-                c[k] = __fmaf_rn(__fadd_rn(static_cast<float>(ci[k]), 0.5f), step, a.aabb_min[k]);
+                const float lo = mip == 0u ? a.casc.bmn[k] : __fsub_rn(a.casc.c[k], __fmul_rn(a.casc.h[k], s));
+                const float step = __fdiv_rn(__fmul_rn(a.casc.bsize[k], s), static_cast<float>(R));
+                c[k] = __fmaf_rn(__fadd_rn(static_cast<float>(ci[k]), 0.5f), step, lo);
             }
             world_to_unit(a, c, u);
         } else {
@@ -867,13 +872,7 @@ __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
     }
     const uint32_t tid = threadIdx.x, lane = tid & 31u, warp = tid >> 5;
     const uint32_t g = lane >> 2, t4 = lane & 3u;
-    AabbConsts box;
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        box.mn[k] = a.aabb_min[k];
-        box.mx[k] = a.aabb_max[k];
-        box.size[k] = a.aabb_size[k];
-    }
+    const AabbConsts box = make_box(a.aabb_min, a.aabb_max, a.aabb_size, a.casc);
     const float cone = cone_angle(a.fx, a.fy);
     // Work enumeration over this rank's tiles.
     const uint32_t tile = a.tile;

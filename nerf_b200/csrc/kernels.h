@@ -39,7 +39,8 @@ struct FieldArgs {
     const float4* pos_dt;
     const uint32_t* sample_ray;
     const RayRecord* rays;
-    float aabb_min[3], aabb_max[3], aabb_size[3];
+    float aabb_min[3], aabb_max[3], aabb_size[3];  // marching box (positions are normalised in it)
+    CascadeBox casc;
     // occupancy rows
     uint32_t grid_res, cell_count, update_count, warmup_steps, update_interval;
     float* occ_sigma;
@@ -219,7 +220,8 @@ struct RenderArgs {
     uint32_t mlp_offset;
     const uint32_t* bitfield;
     uint32_t grid_res;
-    float aabb_min[3], aabb_max[3], aabb_size[3];
+    float aabb_min[3], aabb_max[3], aabb_size[3];  // marching box
+    CascadeBox casc;
     float c2w[12];
     uint32_t width, height;
     float fx, fy, cx, cy;

@@ -13,9 +13,48 @@ struct Ray {
     float tn, tf;
 };
 
+// Marching box and occupancy cascades.  mn / mx / size: the box rays are
+// clipped to and positions are normalised in -- the outermost cascade.
+// Cascade k (k < cascades) covers centre +- half * 2^k; cascade 0 is the
+// configured AABB (bmn, bsize), and with one cascade the marching box is that
+// AABB itself.
 struct AabbConsts {
     float mn[3], mx[3], size[3];
+    float bmn[3], bsize[3], c[3], h[3];
+    uint32_t cascades;
 };
+
+// 2^k as a float (exact, k < 127).
+NB_DEV float pow2f(uint32_t k) { return __int_as_float(static_cast<int>((127u + k) << 23)); }
+
+NB_DEV AabbConsts make_box(const float mn[3], const float mx[3], const float size[3], const CascadeBox& cb) {
+    AabbConsts b;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+        b.mn[k] = mn[k];
+        b.mx[k] = mx[k];
+        b.size[k] = size[k];
+        b.bmn[k] = cb.bmn[k];
+        b.bsize[k] = cb.bsize[k];
+        b.c[k] = cb.c[k];
+        b.h[k] = cb.h[k];
+    }
+    b.cascades = cb.cascades;
+    return b;
+}
+
+// Cascade of a point: 0 inside the configured AABB, else ceil(log2(m)) for
+// m = max_k |p_k - centre_k| / half_k (m = f 2^e with f in [0.5, 1): e, or
+// e - 1 when m is a power of two); cascades or more when outside them all.
+NB_DEV uint32_t cascade_of(const AabbConsts& b, const float p[3]) {
+    float m = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) m = fmaxf(m, __fdiv_rn(fabsf(__fsub_rn(p[k], b.c[k])), b.h[k]));
+    if (!(m > 1.0f)) return 0u;
+    int e = 0;
+    const float f = frexpf(m, &e);
+    return static_cast<uint32_t>(f == 0.5f ? e - 1 : e);
+}
 
 // Camera ray through continuous pixel (px, py); py is measured from the top
 // row and flipped to H-1-py (reference backend-cuda.cu:373-390, 438-441).
@@ -62,36 +101,31 @@ NB_DEV bool clip_aabb(const AabbConsts& b, Ray& r) {
     return __fsub_rn(tf, tn) > 0.0f;
 }
 
-// Occupancy bit of the cell holding p (reference backend-cuda.cu:338-351).
+// Occupancy bit of the cell holding p (reference backend-cuda.cu:338-351),
+// in the R^3 grid of p's cascade (bitfield: cascade after cascade).
 NB_DEV bool occupied(const uint32_t* __restrict__ bits, uint32_t R, const AabbConsts& b, const float p[3]) {
     float rel[3];
+    uint32_t mip = 0u;
+    if (b.cascades <= 1u) {
 #pragma unroll
-    for (int k = 0; k < 3; ++k) rel[k] = __fdiv_rn(__fsub_rn(p[k], b.mn[k]), b.size[k]);
+        for (int k = 0; k < 3; ++k) rel[k] = __fdiv_rn(__fsub_rn(p[k], b.mn[k]), b.size[k]);
+    } else {
+        mip = cascade_of(b, p);
+        if (mip >= b.cascades) return false;
+        const float s = pow2f(mip);
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const float lo = mip == 0u ? b.bmn[k] : __fsub_rn(b.c[k], __fmul_rn(b.h[k], s));
+            rel[k] = __fdiv_rn(__fsub_rn(p[k], lo), __fmul_rn(b.bsize[k], s));
+        }
+    }
     if (rel[0] < 0.0f || rel[0] >= 1.0f || rel[1] < 0.0f || rel[1] >= 1.0f || rel[2] < 0.0f || rel[2] >= 1.0f) return false;
     const float Rf = static_cast<float>(R);
     const uint32_t ix = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[0], Rf)));
     const uint32_t iy = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[1], Rf)));
     const uint32_t iz = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[2], Rf)));
-    const uint32_t idx = ix + iy * R + iz * R * R;
+    const uint32_t idx = mip * R * R * R + ix + iy * R + iz * R * R;
     return ((__ldg(bits + (idx >> 5)) >> (idx & 31u)) & 1u) != 0u;
-}
-
-// Bitfield word of the cell holding p (and the bit within it), or ~0u when p
-// lies outside the box: the address half of occupied(), so that the load can
-// be issued well before its bit is tested.
-NB_DEV uint32_t occupancy_word(uint32_t R, const AabbConsts& b, const float p[3], uint32_t& bit) {
-    float rel[3];
-#pragma unroll
-    for (int k = 0; k < 3; ++k) rel[k] = __fdiv_rn(__fsub_rn(p[k], b.mn[k]), b.size[k]);
-    bit = 0u;
-    if (rel[0] < 0.0f || rel[0] >= 1.0f || rel[1] < 0.0f || rel[1] >= 1.0f || rel[2] < 0.0f || rel[2] >= 1.0f) return 0xFFFFFFFFu;
-    const float Rf = static_cast<float>(R);
-    const uint32_t ix = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[0], Rf)));
-    const uint32_t iy = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[1], Rf)));
-    const uint32_t iz = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[2], Rf)));
-    const uint32_t idx = ix + iy * R + iz * R * R;
-    bit = idx & 31u;
-    return idx >> 5;
 }
 
 // One step of the cone-angle march (reference backend-cuda.cu:455-468):

@@ -35,14 +35,7 @@ __device__ __forceinline__ uint32_t ray_seed(uint32_t frame, uint32_t global_ray
 }
 
 __device__ __forceinline__ AabbConsts aabb_of(const TrainConsts& tc) {
-    AabbConsts b;
-#pragma unroll
-    for (int k = 0; k < 3; ++k) {
-        b.mn[k] = tc.aabb_min[k];
-        b.mx[k] = tc.aabb_max[k];
-        b.size[k] = tc.aabb_size[k];
-    }
-    return b;
+    return make_box(tc.aabb_min, tc.aabb_max, tc.aabb_size, tc.casc);
 }
 
 // Training ray of a step: pixel from the hashed RNG (reference

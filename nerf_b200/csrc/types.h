@@ -101,11 +101,20 @@ struct DpSync {
 };
 
 // Per-step constants of the training graph, passed by value to kernels.
+// Occupancy cascades: cascade k covers centre c +- half h * 2^k; cascade 0 is
+// the configured AABB (min bmn, size bsize).  One cascade: the marching box
+// is that AABB.
+struct CascadeBox {
+    float bmn[3], bsize[3], c[3], h[3];
+    uint32_t cascades;
+};
+
 struct TrainConsts {
     // scene
     uint32_t n_images, width, height, pad_;
     float fx, fy, cx, cy;
-    float aabb_min[3], aabb_max[3], aabb_size[3];
+    float aabb_min[3], aabb_max[3], aabb_size[3];  // marching box (outermost cascade)
+    CascadeBox casc;
     float cone;
     // sampler
     uint32_t max_rays;

@@ -129,6 +129,7 @@ typedef struct OracleOptions {
     uint32_t dp_rank;
     uint32_t dp_world;
     uint32_t n_threads;
+    uint32_t n_cascades;              /* occupancy cascades (0 or 1: the configured AABB only) */
 } OracleOptions;
 
 typedef struct OracleBatchInfo {

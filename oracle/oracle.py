@@ -38,7 +38,7 @@ class Options(C.Structure):
     _fields_ = [("n_levels", U32), ("log2_hashmap_size", U32), ("base_resolution", U32), ("max_resolution", U32),
                 ("hash_init_scale", F32), ("background", U32), ("stop_transmittance", F32),
                 ("target_samples_per_step", U32), ("max_samples_per_step", U32), ("dp_rank", U32), ("dp_world", U32),
-                ("n_threads", U32)]
+                ("n_threads", U32), ("n_cascades", U32)]
 
 
 class BatchInfo(C.Structure):
@@ -210,9 +210,10 @@ def occupancy_cells(frame, update_count, cell_count, grid_res, aabb_min, aabb_ma
 
 def options(n_levels=16, log2_hashmap_size=19, base_resolution=16, max_resolution=2048, hash_init_scale=1e-4,
             background=0, stop_transmittance=1e-4, target_samples_per_step=0, max_samples_per_step=0, dp_rank=0,
-            dp_world=1, n_threads=1) -> Options:
+            dp_world=1, n_threads=1, n_cascades=1) -> Options:
     return Options(n_levels, log2_hashmap_size, base_resolution, max_resolution, hash_init_scale, background,
-                   stop_transmittance, target_samples_per_step, max_samples_per_step, dp_rank, dp_world, n_threads)
+                   stop_transmittance, target_samples_per_step, max_samples_per_step, dp_rank, dp_world, n_threads,
+                   n_cascades)
 
 
 class Context:
@@ -228,6 +229,7 @@ class Context:
         self.n_params = self.lib.oracle_ctx_param_count(self.h, C.byref(ng), C.byref(nm))
         self.n_grid, self.n_mlp = ng.value, nm.value
         self.grid_res = desc.occupancy_grid_res
+        self.cascades = max(1, int(opts.n_cascades))
 
     def close(self):
         if self.h:
@@ -285,7 +287,7 @@ class Context:
         return ls.value, act.value
 
     def occupancy(self):
-        cells = self.grid_res ** 3
+        cells = self.grid_res ** 3 * self.cascades
         d = np.zeros(cells, np.float32)
         b = np.zeros((cells + 31) // 32, np.uint32)
         self.lib.oracle_ctx_get_occupancy(self.h, ptr(d), ptr(b))

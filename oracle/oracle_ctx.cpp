@@ -81,15 +81,68 @@ bool intersect_aabb(const float o[3], const float d[3], const float mn[3], const
     return true;
 }
 
-// Bitfield lookup of the cell holding p (reference backend-cuda.cu:338-351).
-bool occupied(const uint32_t* bits, uint32_t R, const float mn[3], const float size[3], const float p[3]) {
+// Marching box and occupancy cascades: cascade k covers centre c +- half h *
+// 2^k (cascade 0: the configured AABB bmn, bsize); rays are clipped to the
+// outermost cascade (mn, mx, size), which with one cascade is that AABB.
+struct Box {
+    float mn[3], mx[3], size[3];
+    float bmn[3], bsize[3], c[3], h[3];
+    uint32_t K = 1;
+};
+Box make_box(const float amin[3], const float amax[3], uint32_t K) {
+    Box b;
+    b.K = K;
+    for (int k = 0; k < 3; ++k) {
+        b.bmn[k] = amin[k];
+        b.bsize[k] = amax[k] - amin[k];
+        b.c[k] = (amin[k] + amax[k]) * 0.5f;
+        b.h[k] = b.bsize[k] * 0.5f;
+        b.mn[k] = amin[k];
+        b.mx[k] = amax[k];
+    }
+    if (K > 1u) {
+        const float s = std::ldexp(1.0f, static_cast<int>(K) - 1);
+        for (int k = 0; k < 3; ++k) {
+            const float hs = b.h[k] * s;
+            b.mn[k] = b.c[k] - hs;
+            b.mx[k] = b.c[k] + hs;
+        }
+    }
+    for (int k = 0; k < 3; ++k) b.size[k] = b.mx[k] - b.mn[k];
+    return b;
+}
+// Cascade of p: 0 inside the configured AABB, else ceil(log2 m) with
+// m = max_k |p_k - c_k| / h_k (from m = f 2^e, f in [0.5, 1)).
+uint32_t cascade_of(const Box& b, const float p[3]) {
+    float m = 0.0f;
+    for (int k = 0; k < 3; ++k) m = std::fmax(m, std::fabs(p[k] - b.c[k]) / b.h[k]);
+    if (!(m > 1.0f)) return 0u;
+    int e = 0;
+    const float f = std::frexp(m, &e);
+    return static_cast<uint32_t>(f == 0.5f ? e - 1 : e);
+}
+
+// Bitfield lookup of the cell holding p (reference backend-cuda.cu:338-351),
+// in the R^3 grid of p's cascade (cascade after cascade in the bitfield).
+bool occupied(const uint32_t* bits, uint32_t R, const Box& b, const float p[3]) {
     float rel[3];
-    for (int k = 0; k < 3; ++k) rel[k] = (p[k] - mn[k]) / size[k];
+    uint32_t mip = 0;
+    if (b.K <= 1u) {
+        for (int k = 0; k < 3; ++k) rel[k] = (p[k] - b.mn[k]) / b.size[k];
+    } else {
+        mip = cascade_of(b, p);
+        if (mip >= b.K) return false;
+        const float s = std::ldexp(1.0f, static_cast<int>(mip));
+        for (int k = 0; k < 3; ++k) {
+            const float lo = mip == 0u ? b.bmn[k] : b.c[k] - b.h[k] * s;
+            rel[k] = (p[k] - lo) / (b.bsize[k] * s);
+        }
+    }
     for (int k = 0; k < 3; ++k)
         if (rel[k] < 0.0f || rel[k] >= 1.0f) return false;
     uint32_t ix[3];
     for (int k = 0; k < 3; ++k) ix[k] = std::min(R - 1u, static_cast<uint32_t>(rel[k] * static_cast<float>(R)));
-    const uint32_t idx = ix[0] + ix[1] * R + ix[2] * R * R;
+    const uint32_t idx = mip * R * R * R + ix[0] + ix[1] * R + ix[2] * R * R;
     return ((bits[idx >> 5] >> (idx & 31u)) & 1u) != 0u;
 }
 
@@ -103,8 +156,7 @@ float cone_angle(float fx, float fy) {
 //   dt = min(max(dt_min, t*cone), t_far - t), t_mid = t + dt/2, p = fma(t_mid, d, o),
 //   keep the step when p's cell is occupied, t += dt, at most max_steps steps.
 template <class F>
-uint32_t march(const Ray& r, uint32_t max_steps, float cone, const float mn[3], const float size[3], uint32_t R,
-               const uint32_t* bits, F&& on_sample) {
+uint32_t march(const Ray& r, uint32_t max_steps, float cone, const Box& box, uint32_t R, const uint32_t* bits, F&& on_sample) {
     const float dt_min = (r.tf - r.tn) / static_cast<float>(max_steps);
     float t = r.tn;
     uint32_t i = 0, count = 0;
@@ -113,7 +165,7 @@ uint32_t march(const Ray& r, uint32_t max_steps, float cone, const float mn[3], 
         const float t_mid = t + 0.5f * dt;
         float p[3];
         for (int k = 0; k < 3; ++k) p[k] = std::fmaf(t_mid, r.d[k], r.o[k]);
-        if (occupied(bits, R, mn, size, p)) {
+        if (occupied(bits, R, box, p)) {
             on_sample(i, t_mid, dt, p);
             ++count;
         }
@@ -142,7 +194,8 @@ struct Ctx {
     // configuration
     bool configured = false;
     NerfTrainingConfig cfg{};
-    float mn[3] = {0, 0, 0}, mx[3] = {1, 1, 1}, size[3] = {1, 1, 1};
+    float mn[3] = {0, 0, 0}, mx[3] = {1, 1, 1}, size[3] = {1, 1, 1};  // marching box
+    Box box = make_box(mn, mx, 1);
     uint32_t cell_count = 0, update_count = 0, cap = 0;
     // step state
     uint32_t frame = 0, n_rays = 0;
@@ -230,15 +283,20 @@ void occupancy_apply(float* density, uint32_t* bits, const float* sig, uint32_t 
 // World position of the k-th queried cell of an occupancy refresh: cells
 // are visited round-robin from frame * update_count mod C, the query point is
 // the cell centre (reference backend-cuda.cu:1575-1616).
-void occupancy_cell_center(uint32_t frame, uint32_t k, uint32_t update_count, uint32_t cell_count, uint32_t R,
-                           const float mn[3], const float mx[3], float c[3]) {
+// With cascades the cells run cascade after cascade, each centre in its
+// cascade's box.
+void occupancy_cell_center(uint32_t frame, uint32_t k, uint32_t update_count, uint32_t cell_count, uint32_t R, const Box& b,
+                           float c[3]) {
     const uint32_t start = static_cast<uint32_t>(static_cast<uint64_t>(frame) * update_count % cell_count);
-    const uint32_t cell = static_cast<uint32_t>((static_cast<uint64_t>(start) + k) % cell_count);
+    const uint32_t q = static_cast<uint32_t>((static_cast<uint64_t>(start) + k) % cell_count);
+    const uint32_t mip = q / (R * R * R), cell = q - mip * R * R * R;
     const uint32_t z = cell / (R * R), rem = cell - z * R * R, y = rem / R, x = rem - y * R;
     const uint32_t ci[3] = {x, y, z};
+    const float s = std::ldexp(1.0f, static_cast<int>(mip));
     for (int d = 0; d < 3; ++d) {
-        const float step = (mx[d] - mn[d]) / static_cast<float>(R);
-        c[d] = std::fmaf(static_cast<float>(ci[d]) + 0.5f, step, mn[d]);
+        const float lo = mip == 0u ? b.bmn[d] : b.c[d] - b.h[d] * s;
+        const float step = (b.bsize[d] * s) / static_cast<float>(R);
+        c[d] = std::fmaf(static_cast<float>(ci[d]) + 0.5f, step, lo);
     }
 }
 
@@ -253,7 +311,7 @@ void Ctx::occupancy_step(uint32_t mode) {
         parallel_for(update_count, opt.n_threads, [&](uint64_t b, uint64_t e, uint32_t) {
             for (uint64_t k = b; k < e; ++k) {
                 float c[3];
-                occupancy_cell_center(frame, static_cast<uint32_t>(k), update_count, cell_count, grid_res, mn, mx, c);
+                occupancy_cell_center(frame, static_cast<uint32_t>(k), update_count, cell_count, grid_res, box, c);
                 float u[3];
                 to_unit(c, u);
                 uint16_t feat[64];
@@ -293,11 +351,11 @@ void Ctx::sample_batch(uint32_t camera) {
             const float pyf = static_cast<float>(H) - 1.0f - ray.py;
             for (int k = 0; k < 3; ++k) ray.o[k] = cam[4 * k + 3];
             if (!ray_dir(cam, fx, fy, cx, cy, ray.px, pyf, ray.d)) continue;
-            if (!intersect_aabb(ray.o, ray.d, mn, mx, &ray.tn, &ray.tf)) continue;
+            if (!intersect_aabb(ray.o, ray.d, box.mn, box.mx, &ray.tn, &ray.tf)) continue;
             if (!(ray.tf - ray.tn > 0.0f)) continue;
             rays[r] = ray;
             ok[r] = 1;
-            ray_counts[r] = march(ray, max_steps, cone, mn, size, grid_res, bits.data(),
+            ray_counts[r] = march(ray, max_steps, cone, box, grid_res, bits.data(),
                                   [](uint32_t, float, float, const float*) {});
         }
     });
@@ -326,7 +384,7 @@ void Ctx::sample_batch(uint32_t camera) {
             const uint32_t r = k_index[k];
             const Ray& ray = rays[r];
             uint32_t s = k_begin[k];
-            march(ray, max_steps, cone, mn, size, grid_res, bits.data(),
+            march(ray, max_steps, cone, box, grid_res, bits.data(),
                   [&](uint32_t, float, float dt, const float* p) {
                       s_pos[4ull * s + 0] = p[0];
                       s_pos[4ull * s + 1] = p[1];
@@ -497,7 +555,8 @@ void* oracle_ctx_create(const NerfCreateDesc* desc, const OracleOptions* opt) {
     c->grid_res = desc->occupancy_grid_res;
     c->max_sample_steps = desc->max_sample_steps;
     c->max_batch_rays = desc->max_batch_rays;
-    c->cell_count = c->grid_res * c->grid_res * c->grid_res;
+    if (c->opt.n_cascades == 0u) c->opt.n_cascades = 1u;
+    c->cell_count = c->grid_res * c->grid_res * c->grid_res * c->opt.n_cascades;
     c->density.assign(c->cell_count, 0.0f);
     c->bits.assign((c->cell_count + 31u) / 32u, 0u);
     c->init_params();
@@ -519,7 +578,12 @@ int oracle_ctx_configure(void* ctx, const NerfTrainingConfig* cfg) {
     c->mx[0] = cfg->aabb_max_x;
     c->mx[1] = cfg->aabb_max_y;
     c->mx[2] = cfg->aabb_max_z;
-    for (int k = 0; k < 3; ++k) c->size[k] = c->mx[k] - c->mn[k];
+    c->box = make_box(c->mn, c->mx, c->opt.n_cascades);
+    for (int k = 0; k < 3; ++k) {  // the marching box: the outermost cascade
+        c->mn[k] = c->box.mn[k];
+        c->mx[k] = c->box.mx[k];
+        c->size[k] = c->box.size[k];
+    }
     c->update_count = std::min(cfg->occupancy_params.cells_per_update, c->cell_count);
     const uint64_t want = c->opt.max_samples_per_step
                               ? c->opt.max_samples_per_step
@@ -611,7 +675,8 @@ int oracle_ctx_set_grads(void* ctx, const float* grad, float loss_sum, uint32_t 
 
 void oracle_occupancy_cells(uint32_t frame, uint32_t update_count, uint32_t cell_count, uint32_t grid_res, const float* mn,
                             const float* mx, float* out_xyz) {
-    for (uint32_t k = 0; k < update_count; ++k) occupancy_cell_center(frame, k, update_count, cell_count, grid_res, mn, mx, out_xyz + 3ull * k);
+    const Box b = make_box(mn, mx, 1u);
+    for (uint32_t k = 0; k < update_count; ++k) occupancy_cell_center(frame, k, update_count, cell_count, grid_res, b, out_xyz + 3ull * k);
 }
 
 int oracle_ctx_get_loss(void* ctx, float* loss_sum, uint32_t* active_rays) {
@@ -692,7 +757,7 @@ int oracle_ctx_render(void* ctx, const float* c2w12, uint32_t width, uint32_t he
                              intersect_aabb(ray.o, ray.d, c->mn, c->mx, &ray.tn, &ray.tf) && (ray.tf - ray.tn > 0.0f);
             if (hit) {
                 bool stopped = false;
-                march(ray, max_steps, cone, c->mn, c->size, c->grid_res, c->bits.data(),
+                march(ray, max_steps, cone, c->box, c->grid_res, c->bits.data(),
                       [&](uint32_t, float, float dt, const float* p) {
                           if (stopped) return;
                           if (stop_T > 0.0f && T < stop_T) {

@@ -21,11 +21,11 @@ RAYS, STEPS, RES = 512, 96, 32
 
 
 def make_pair(stop=0.0, background=0, warmup=4, interval=2, log2T=15, n_views=8, size=48, rays=RAYS, steps=STEPS,
-              res=RES, cells=None, target=0, max_samples=0):
+              res=RES, cells=None, target=0, max_samples=0, cascades=1):
     ds = nerf_b200.make_scene(kind=0, seed=0, n_views=n_views, width=size, height=size, fov=0.69, radius=3.0)
     opts = nerf_b200.default_options(log2_hashmap_size=log2T, max_resolution=512, stop_transmittance=stop,
                                      background=background, target_samples_per_step=target,
-                                     max_samples_per_step=max_samples)
+                                     max_samples_per_step=max_samples, n_cascades=cascades)
     ctx = nerf_b200.Context(ds, grid_res=res, max_sample_steps=max(rays * steps, max_samples), max_batch_rays=4 * rays,
                             options=opts)
     cfg = nerf_b200.training_config(rays=rays, steps=steps, warmup=warmup, update_interval=interval,
@@ -33,7 +33,7 @@ def make_pair(stop=0.0, background=0, warmup=4, interval=2, log2T=15, n_views=8,
     ctx.configure(cfg)
     oc = oracle.Context(ctx.desc, oracle.options(log2_hashmap_size=log2T, max_resolution=512, stop_transmittance=stop,
                                                  background=background, target_samples_per_step=target,
-                                                 max_samples_per_step=max_samples, n_threads=8),
+                                                 max_samples_per_step=max_samples, n_threads=8, n_cascades=cascades),
                         ctx._images, ctx._cams)
     oc.configure(cfg)
     return ds, ctx, oc, cfg
@@ -147,6 +147,65 @@ def test_sampler_bit_exact_with_given_bitfield(cuda):
     oc.step()
     g = compare_batch(ctx, oc)
     assert (g["counts"] == 0).any()
+    ctx.close()
+
+
+def test_cascades_sampler_bit_exact_with_given_bitfield(cuda):
+    """Three occupancy cascades (the configured box [-1,1]^3 scaled by 1, 2, 4; cameras at radius 3 start inside the
+    outermost): per-ray counts, compaction and sample positions bit-exact against the oracle over a sparse random
+    bitfield of all three cascades, with samples in every cascade."""
+    _, ctx, oc, _ = make_pair(warmup=1, interval=1000, cascades=3)
+    rng = np.random.default_rng(22)
+    words = (3 * RES ** 3 + 31) // 32
+    bits = (rng.integers(0, 2 ** 32, words, dtype=np.uint64) & rng.integers(0, 2 ** 32, words, dtype=np.uint64)).astype(np.uint32)
+    ctx.set_occupancy(bitfield=bits)
+    ctx.set_frame(5)
+    oc.set_occupancy(bits=bits)
+    oc.set_frame(5)
+    oc.set_params(ctx.params()[0])
+    ctx.train_step()
+    oc.step()
+    g = compare_batch(ctx, oc)
+    m = np.abs(g["pos_dt"][:, :3]).max(axis=1)
+    assert (m <= 1).any() and ((m > 1) & (m <= 2)).any() and (m > 2).any()
+    ctx.close()
+
+
+def test_cascades_occupancy_refresh(cuda):
+    """Occupancy refreshes over three cascades (cell centres cascade after cascade): densities as in the single-grid
+    test, bitfield bit-exact except at the threshold, and the next steps' samples bit-exact."""
+    _, ctx, oc, _ = make_pair(warmup=2, interval=2, cascades=3, cells=3 * RES ** 3 // 2)
+    for _ in range(2):
+        ctx.train_step()
+    for step in range(3):  # frames 2..4: refresh on 2 and 4
+        sync_oracle(ctx, oc)
+        ctx.train_step()
+        oc.step()
+        compare_batch(ctx, oc)
+        gd, gb = ctx.occupancy()
+        od, ob = oc.occupancy()
+        assert gd.shape == (3 * RES ** 3,)
+        assert np.allclose(gd, od, rtol=2e-2, atol=1e-4)
+        mismatch = np.unpackbits((gb ^ ob).view(np.uint8), bitorder="little")[: 3 * RES ** 3]
+        near = np.abs(od - 0.01) < 2e-2 * 0.01 + 1e-4
+        assert not (mismatch.astype(bool) & ~near).any()
+    ctx.close()
+
+
+def test_cascades_render_matches_oracle(cuda):
+    ds, ctx, oc, _ = make_pair(warmup=2, interval=1, cascades=2)
+    for _ in range(5):
+        ctx.train_step()
+    sync_oracle(ctx, oc)
+    W = H = 32
+    fx, fy, cx, cy = ds.intrinsics
+    s = W / ds.width
+    intr = (fx * s, fy * s, (W - 1) / 2, (H - 1) / 2)
+    img = np.zeros((H, W, 4), np.uint8)
+    ctx.render(ds.cameras[2], W, H, intr, max_steps=STEPS, stop=1e-4, dst=img)
+    rgba, _ = oc.render(ds.cameras[2], W, H, intr, STEPS, 1e-4)
+    diff = np.abs(img.astype(int) - rgba.view(np.uint8).reshape(H, W, 4).astype(int))
+    assert diff.max() <= 2 and diff.mean() < 0.1
     ctx.close()
 
 
