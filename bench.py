@@ -50,19 +50,48 @@ AABB2 = ((-1.5, -1.5, -1.5), (1.5, 1.5, 1.5))
 TARGET_SAMPLES = 1 << 18
 MAX_STEPS_PER_RAY = 1024
 GRID_RES = 128
+# BASELINE config 4 (large unbounded-style scene; `--config 4`): 40 spheres/boxes on a ground slab inside a sky shell
+# at radius 12, cameras on a radius-3 ring at height 0.3 looking outward and inward, 1920x1080 (300 views in the
+# configuration; --views sets the count, default 60); five 128^3 occupancy cascades over the AABB [-1,1]^3 scaled by
+# up to 16; hash grid L16 F2 T2^22 N_max 8192.  The field of view is not given by the configuration: 1.2 rad.
+CFG4 = dict(kind=2, seed=4, n_primitives=40, density=100.0, extent=6.0, size_min=0.1, size_max=0.6, n_views=60,
+            width=1920, height=1080, fov=1.2, radius=3.0, camera_mode=3, orbit_elevation=0.3, orbit_views=300)
+AABB4 = ((-1.0, -1.0, -1.0), (1.0, 1.0, 1.0))
+CASCADES4 = 5
+CONFIG = 2  # the workload bench.py runs (main() sets it from --config)
 WORKLOAD = ("config2 bounded training: 12 spheres/boxes, 100 views 800x800, hash L16 F2 T2^19 Nmax2048, "
             "2^18 target samples/step/GPU, <=1024 steps/ray, 128^3 occupancy every 16 steps, random bg")
 
 
+WORKLOAD4 = ("config4 unbounded-style training: 40 spheres/boxes on a ground slab, sky shell r=12, 1920x1080 ring views, "
+             "hash L16 F2 T2^22 Nmax8192, 5 occupancy cascades of 128^3 (scale 16), 2^18 target samples/step/GPU, "
+             "<=1024 steps/ray, one cascade's worth of cells refreshed every 16 steps, random bg")
+
+
+def workload_name():
+    return WORKLOAD4 if CONFIG == 4 else WORKLOAD
+
+
 def options(nb, **kw):
+    if CONFIG == 4:
+        return nb.default_options(log2_hashmap_size=22, max_resolution=8192, background=1, stop_transmittance=1e-4,
+                                  target_samples_per_step=TARGET_SAMPLES, max_samples_per_step=2 * TARGET_SAMPLES,
+                                  n_cascades=CASCADES4, **kw)
     return nb.default_options(log2_hashmap_size=19, max_resolution=2048, background=1, stop_transmittance=1e-4,
                               target_samples_per_step=TARGET_SAMPLES, max_samples_per_step=2 * TARGET_SAMPLES, **kw)
 
 
 def train_config(nb):
-    return nb.training_config(aabb=AABB2, rays=4096, steps=MAX_STEPS_PER_RAY, lr=1e-2, beta1=0.9, beta2=0.99,
-                              eps=1e-15, clip=1e9, guard=1e12, loss_scale=128.0, lr_decay_ksteps=0, decay=0.95,
-                              threshold=0.01, cells_per_update=GRID_RES ** 3, update_interval=16, warmup=256)
+    # config 4: 5 x 128^3 cells; each refresh queries 128^3 of them (round robin), so every cell is refreshed every
+    # 80 steps
+    return nb.training_config(aabb=AABB4 if CONFIG == 4 else AABB2, rays=4096, steps=MAX_STEPS_PER_RAY, lr=1e-2,
+                              beta1=0.9, beta2=0.99, eps=1e-15, clip=1e9, guard=1e12, loss_scale=128.0,
+                              lr_decay_ksteps=0, decay=0.95, threshold=0.01, cells_per_update=GRID_RES ** 3,
+                              update_interval=16, warmup=256)
+
+
+def scene_cfg():
+    return CFG4 if CONFIG == 4 else CFG2
 
 
 def peaks():
@@ -134,9 +163,11 @@ class ClockSampler:
 
 
 def make_dataset(nb, views=None):
-    cfg = dict(CFG2)
+    cfg = dict(scene_cfg())
     if views is not None:
         cfg["n_views"] = views
+    if CONFIG == 4:  # the ring is shared out over the views actually rendered
+        cfg["orbit_views"] = cfg["n_views"]
     t0 = time.time()
     ds = nb.make_scene(**cfg)
     return ds, time.time() - t0
@@ -261,11 +292,11 @@ def run_ours(args):
         hbm, src = peaks()
         dom = max(kernels, key=lambda k: k["ms"])
         line = {
-            "metric": "train samples/s (config 2, steady state)",
+            "metric": f"train samples/s (config {CONFIG}, steady state)",
             "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16 (fp32 accumulate, fp32 Adam masters)", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "parallelism": f"dp{world}", "pretrain_steps": args.pretrain,
+            "config": {"workload": workload_name(), "parallelism": f"dp{world}", "pretrain_steps": args.pretrain,
                        "samples_per_step": samples_all / args.steps, "rays_per_step": rays_all / args.steps,
                        "l2": "inputs larger than L2: each step streams the 171 MB fp32 master/m/v through Adam and "
                              "reads a 256 MB image set; the 24 MB hash table is meant to stay L2-resident",
@@ -292,7 +323,7 @@ def kernel_table(ctx, prof_ms, samples):
     from nerf_b200 import abi
     n_params = ctx.n_params
     n_grid = ctx.n_grid
-    cells = GRID_RES ** 3
+    cells = GRID_RES ** 3 * (CASCADES4 if CONFIG == 4 else 1)
     per = {
         # stored features 64 + dout 16 + pos/dt 16 + ray id 4, and 128 f16x2 read-modify-writes of 4+4 bytes
         "field_backward": samples * (64 + 16 + 16 + 4 + 128 * 8),
@@ -377,13 +408,18 @@ def roofline(dom, hbm, src):
 
 
 def psnr_heldout(nb, ctx, args):
-    """PSNR of the trained model on held-out views of the config-2 scene (cameras after the 100 training views,
-    ground truth composited on white, the render's background)."""
+    """PSNR of the trained model on held-out views (config 2: cameras after the 100 training views; config 4: ring
+    positions between the training views), ground truth composited on white, the render's background."""
     n = args.psnr_views
     if n <= 0:
         return None
-    held = nb.make_scene(**{**CFG2, "n_views": n, "view_offset": CFG2["n_views"], "orbit_views": CFG2["n_views"] + n})
-    W, H = CFG2["width"], CFG2["height"]
+    sc = scene_cfg()
+    if CONFIG == 4:  # ring positions halfway between training views, and training positions looking the other way
+        n_train = args.views or sc["n_views"]
+        held = nb.make_scene(**{**sc, "n_views": n, "view_offset": 1, "orbit_views": 2 * n_train})
+    else:
+        held = nb.make_scene(**{**sc, "n_views": n, "view_offset": sc["n_views"], "orbit_views": sc["n_views"] + n})
+    W, H = sc["width"], sc["height"]
     errs = []
     img = np.zeros((H, W, 4), np.uint8)
     for v in range(n):
@@ -774,6 +810,8 @@ def main():
     ap.add_argument("--skip-cpu", action="store_true")
     ap.add_argument("--skip-reference-cuda", action="store_true")
     ap.add_argument("--skip-dataset-io", action="store_true")
+    ap.add_argument("--config", type=int, default=2, choices=[2, 4],
+                    help="2: bounded training (the headline); 4: the large unbounded-style scene with cascades")
     ap.add_argument("--micro", action="store_true", help="kernel microbench sweep (config 5) instead of the step")
     ap.add_argument("--micro-reps", type=int, default=10)
     ap.add_argument("--micro-points", type=int, nargs="*", default=[20, 22, 24])
@@ -784,6 +822,16 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    global CONFIG
+    CONFIG = args.config
+    if CONFIG == 4:  # config-2-only legs: the render (config 3), the e2e job, the CPU oracle, the dataset files
+        args.skip_render = args.skip_e2e = args.skip_cpu = args.skip_dataset_io = True
+        if args.psnr_views == 20:
+            args.psnr_views = 4
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "config 4 needs occupancy cascades and an AABB of "
+                              "scale 16, which the reference backend does not have (one [0,1]^3 grid)"}), flush=True)
+            return
     if args.micro:
         run_micro(args)
     elif args.impl == "reference":

@@ -179,10 +179,15 @@ NERF_API NerfStatus nerf_b200_render_output(void* context, const void** device_r
 /* ------------------------------------------------------ synthetic scenes */
 /* Seeded procedural scenes and their exact ground-truth renders (host code),
  * standing in for the Blender datasets: kind 0 = spheres of constant colour,
- * kind 1 = spheres and boxes with value-noise albedo.  Writes n_views RGBA8
- * images (NULL: cameras only), row-major 4x4 camera-to-world matrices and
- * (fx, fy, cx, cy).  camera_mode: 0 sphere, 1 upper hemisphere, 2 circular
- * orbit of orbit_views views at orbit_elevation (radians). */
+ * kind 1 = spheres and boxes with value-noise albedo, kind 2 = an
+ * unbounded-style scene (n_primitives spheres and boxes standing on a ground
+ * slab over [-12, 12]^2, centres within +-extent, inside a sky shell of radii
+ * 12 to 12.5, value-noise albedo).  Writes n_views RGBA8 images (NULL:
+ * cameras only), row-major 4x4 camera-to-world matrices and (fx, fy, cx, cy).
+ * camera_mode: 0 sphere, 1 upper hemisphere, 2 circular orbit of orbit_views
+ * views at orbit_elevation (radians), 3 ring of orbit_views cameras of the
+ * given radius at height orbit_elevation looking outward (even views) and
+ * inward (odd views). */
 typedef struct NerfB200SceneDesc {
     uint32_t kind;
     uint32_t seed;

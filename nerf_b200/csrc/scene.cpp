@@ -6,6 +6,10 @@
 //   kind 0: spheres of constant density and colour (smoke configuration)
 //   kind 1: spheres and axis-aligned boxes of constant density whose albedo
 //           is 3-octave value noise (bounded training configuration)
+//   kind 2: an unbounded-style scene: spheres and boxes standing on a ground
+//           slab, inside a sky shell (radii 12 to 12.5), all with
+//           value-noise albedo (large-scene configuration; the shell's density
+//           is constant, so the renders stay exact)
 // Density is piecewise constant along a ray, so the renderer integrates it
 // exactly: the ray is cut at every primitive boundary, each segment has
 // opacity 1 - exp(-sigma * length) and colour (kind 0) the density-weighted
@@ -42,10 +46,12 @@ struct Rng {
 };
 
 struct Prim {
-    int box;           // 0 sphere, 1 box
+    int box;           // 0 sphere, 1 box, 2 spherical shell (r to r2)
     double c[3];
-    double r;          // sphere radius or box half-size
+    double r;          // sphere radius, box half-size (all axes unless hs is set), shell inner radius
     double rgb[3];
+    double hs[3] = {0, 0, 0};  // box half-sizes per axis (when non-zero)
+    double r2 = 0.0;           // shell outer radius
 };
 
 struct Scene {
@@ -88,7 +94,26 @@ void albedo(uint32_t seed, const double p[3], double out[3]) {
     }
 }
 
+bool ray_sphere(const double c[3], double r, const double o[3], const double d[3], double& t0, double& t1) {
+    double oc[3] = {o[0] - c[0], o[1] - c[1], o[2] - c[2]};
+    const double b = oc[0] * d[0] + oc[1] * d[1] + oc[2] * d[2];
+    const double cc = oc[0] * oc[0] + oc[1] * oc[1] + oc[2] * oc[2] - r * r;
+    const double disc = b * b - cc;
+    if (disc <= 0.0) return false;
+    const double s = std::sqrt(disc);
+    t0 = -b - s;
+    t1 = -b + s;
+    return true;
+}
+
 bool ray_prim(const Prim& pr, const double o[3], const double d[3], double& t0, double& t1) {
+    if (pr.box == 2) {  // shell seen from inside its inner sphere: from the inner exit to the outer exit
+        double a0, a1, b0, b1;
+        if (!ray_sphere(pr.c, pr.r, o, d, a0, a1) || !ray_sphere(pr.c, pr.r2, o, d, b0, b1)) return false;
+        t0 = std::max(a1, 0.0);
+        t1 = b1;
+        return t1 > t0;
+    }
     if (!pr.box) {
         double oc[3] = {o[0] - pr.c[0], o[1] - pr.c[1], o[2] - pr.c[2]};
         const double b = oc[0] * d[0] + oc[1] * d[1] + oc[2] * d[2];
@@ -102,7 +127,8 @@ bool ray_prim(const Prim& pr, const double o[3], const double d[3], double& t0, 
         t0 = -1e30;
         t1 = 1e30;
         for (int k = 0; k < 3; ++k) {
-            const double lo = pr.c[k] - pr.r, hi = pr.c[k] + pr.r;
+            const double h = pr.hs[k] > 0.0 ? pr.hs[k] : pr.r;
+            const double lo = pr.c[k] - h, hi = pr.c[k] + h;
             if (std::fabs(d[k]) < 1e-12) {
                 if (o[k] < lo || o[k] > hi) return false;
                 continue;
@@ -172,6 +198,34 @@ Scene make_scene(const NerfB200SceneDesc& s) {
     sc.seed = s.seed;
     sc.density = s.density;
     Rng rng(0x5eed0000ull + s.seed);
+    if (s.kind == 2u) {
+        // Ground slab z in [-0.1, 0] over [-12, 12]^2, primitives standing on it
+        // with centres uniform in [-extent, extent]^2, the sky shell around all.
+        Prim ground{};
+        ground.box = 1;
+        ground.c[0] = ground.c[1] = 0.0;
+        ground.c[2] = -0.05;
+        ground.hs[0] = ground.hs[1] = 12.0;
+        ground.hs[2] = 0.05;
+        sc.prims.push_back(ground);
+        const uint32_t n = std::min<uint32_t>(s.n_primitives, 60u);
+        for (uint32_t i = 0; i < n; ++i) {
+            Prim p{};
+            p.box = static_cast<int>(i & 1u);
+            const double size = rng.range(s.size_min, s.size_max);
+            p.r = p.box ? 0.5 * size : size;
+            p.c[0] = rng.range(-s.extent, s.extent);
+            p.c[1] = rng.range(-s.extent, s.extent);
+            p.c[2] = p.r;
+            sc.prims.push_back(p);
+        }
+        Prim sky{};
+        sky.box = 2;
+        sky.r = 12.0;
+        sky.r2 = 12.5;
+        sc.prims.push_back(sky);
+        return sc;
+    }
     const uint32_t n = std::min<uint32_t>(s.n_primitives, 64u);
     for (uint32_t i = 0; i < n; ++i) {
         Prim p{};
@@ -204,6 +258,32 @@ void look_at(const double eye[3], float* m) {
     }
     m[12] = m[13] = m[14] = 0.0f;
     m[15] = 1.0f;
+}
+
+// Camera of mode 3: on a ring of the given radius at height orbit_elevation
+// (a length here), looking outward (even views) or inward (odd views) along
+// the horizontal; returns false for the other modes.
+bool ring_camera(const NerfB200SceneDesc& s, uint32_t view, float* m) {
+    if (s.camera_mode != 3u) return false;
+    const double az = 2.0 * M_PI * view / std::max<uint32_t>(1u, s.orbit_views);
+    const double eye[3] = {s.radius * std::cos(az), s.radius * std::sin(az), s.orbit_elevation};
+    const double sign = (view & 1u) ? -1.0 : 1.0;
+    const double fwd[3] = {sign * std::cos(az), sign * std::sin(az), 0.0};
+    const double z[3] = {-fwd[0], -fwd[1], -fwd[2]};  // camera looks down -z
+    const double up[3] = {0, 0, 1};
+    double x[3] = {up[1] * z[2] - up[2] * z[1], up[2] * z[0] - up[0] * z[2], up[0] * z[1] - up[1] * z[0]};
+    const double n = std::sqrt(x[0] * x[0] + x[1] * x[1] + x[2] * x[2]);
+    for (double& v : x) v /= n;
+    const double y[3] = {z[1] * x[2] - z[2] * x[1], z[2] * x[0] - z[0] * x[2], z[0] * x[1] - z[1] * x[0]};
+    for (int r = 0; r < 3; ++r) {
+        m[4 * r + 0] = static_cast<float>(x[r]);
+        m[4 * r + 1] = static_cast<float>(y[r]);
+        m[4 * r + 2] = static_cast<float>(z[r]);
+        m[4 * r + 3] = static_cast<float>(eye[r]);
+    }
+    m[12] = m[13] = m[14] = 0.0f;
+    m[15] = 1.0f;
+    return true;
 }
 
 void camera_eye(const NerfB200SceneDesc& s, uint32_t view, double eye[3]) {
@@ -244,6 +324,7 @@ NERF_API NerfStatus nerf_b200_scene_render(const NerfB200SceneDesc* s, uint8_t* 
     intrinsics[2] = static_cast<float>(cxp);
     intrinsics[3] = static_cast<float>(cyp);
     for (uint32_t v = 0; v < s->n_views; ++v) {
+        if (ring_camera(*s, s->view_offset + v, cams + 16ull * v)) continue;
         double eye[3];
         camera_eye(*s, s->view_offset + v, eye);
         look_at(eye, cams + 16ull * v);
