@@ -431,8 +431,9 @@ def psnr_heldout(nb, ctx, args):
     psnr = [10.0 * np.log10(1.0 / max(e, 1e-12)) for e in errs]
     return {"value": float(np.mean(psnr)), "unit": "dB", "views": n, "resolution": f"{W}x{H}",
             "train_steps": args.pretrain + 2 * args.warmup + args.steps,
-            "note": "mean over held-out views (the 20 cameras after the training views) of PSNR against the exact "
-                    "render composited on white; rendered with the training occupancy grid, T < 1e-4 termination"}
+            "note": "mean over held-out views (config 2: the cameras after the training views; config 4: ring "
+                    "positions between the training views) of PSNR against the exact render composited on white; "
+                    "rendered with the training occupancy grid, T < 1e-4 termination"}
 
 
 def run_render(nb, ctx, rank, world, args):
