@@ -6,8 +6,8 @@
 //                   fp16 hash-table gradients, fp32 MLP gradients (+ loss
 //                   slot), the device step state
 //   occupancy arena density grid (padded to whole 32-cell words), bitfield
-//   batch arena     (sized at nerf_configure_training) per-ray counts and
-//                   step bitmasks, compacted rays and samples, hash
+//   batch arena     (sized at nerf_configure_training) per-ray counts,
+//                   chunk starts and kept-step lists, compacted rays and samples, hash
 //                   features, raw field outputs and their gradients, the
 //                   backward kernel's weight-gradient partials, the
 //                   occupancy query window
@@ -216,8 +216,8 @@ struct Context {
     bool occupancy_valid = false;
     // batch
     uint32_t* ray_counts = nullptr;
-    uint32_t* masks = nullptr;
-    float* steps_t = nullptr;
+    float* kept_t = nullptr;
+    float* chunk_t = nullptr;
     RayGeom* geom = nullptr;
     uint32_t* ray_offset = nullptr;
     uint32_t* ray_slot = nullptr;
@@ -535,8 +535,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     fwd_blocks = field_forward_blocks();
     batch.align = model.align;
     batch.size = 0;
-    const uint64_t o_rc = batch.add(2ull * t.max_rays * 4ull), o_mask = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
-    const uint64_t o_st = batch.add(static_cast<uint64_t>(t.max_steps) * t.max_rays * 4u);
+    const uint64_t o_rc = batch.add(2ull * t.max_rays * 4ull), o_kept = batch.add(static_cast<uint64_t>(t.max_steps) * t.max_rays * 4u);
+    const uint64_t o_st = batch.add(static_cast<uint64_t>(t.mask_words) * t.max_rays * 4u);
     const uint64_t o_geom = batch.add(t.max_rays * sizeof(RayGeom));
     const uint64_t o_bs = batch.add(t.max_rays * 4ull), o_ba = batch.add(t.max_rays * 4ull);
     const uint64_t o_rays = batch.add(t.max_rays * sizeof(RayRecord)), o_ri = batch.add(t.max_rays * 4ull);
@@ -548,8 +548,8 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     const uint64_t o_gsum = batch.add(own_max * 4u);
     if (batch.alloc() != cudaSuccess) return NERF_STATUS_FAILURE;
     ray_counts = batch.at<uint32_t>(o_rc);
-    masks = batch.at<uint32_t>(o_mask);
-    steps_t = batch.at<float>(o_st);
+    kept_t = batch.at<float>(o_kept);
+    chunk_t = batch.at<float>(o_st);
     geom = batch.at<RayGeom>(o_geom);
     ray_offset = batch.at<uint32_t>(o_bs);
     ray_slot = batch.at<uint32_t>(o_ba);
@@ -597,8 +597,8 @@ SamplerArgs Context::sampler_args() const {
     sa.images = images;
     sa.bitfield = bitfield;
     sa.ray_counts = ray_counts;
-    sa.masks = masks;
-    sa.steps_t = steps_t;
+    sa.kept_t = kept_t;
+    sa.chunk_t = chunk_t;
     sa.geom = geom;
     sa.ray_offset = ray_offset;
     sa.ray_slot = ray_slot;

@@ -110,8 +110,8 @@ struct SamplerArgs {
     const uint8_t* images;
     const uint32_t* bitfield;
     uint32_t* ray_counts;     // [2][max_rays], half (frame & 1) belongs to the step of that frame
-    uint32_t* masks;          // [max_rays][mask_words] occupancy bits of 32 consecutive steps
-    float* steps_t;           // [max_rays][max_steps] t at the start of each step
+    float* kept_t;            // [max_rays][max_steps] t of the ray's kept steps, in step order
+    float* chunk_t;           // [max_rays][mask_words] t at the start of each 32-step chunk
     RayGeom* geom;            // [max_rays]
     uint32_t* ray_offset;     // [max_rays] exclusive sample prefix
     uint32_t* ray_slot;       // [max_rays] compacted index, or ~0 when not kept

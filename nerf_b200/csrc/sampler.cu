@@ -8,16 +8,16 @@
 // one serial part of the march -- the step recurrence t += dt(t) -- is
 // separated from everything that can run in parallel:
 //   k_march        one thread per ray: the ray, its chord and the step
-//                  recurrence, writing t at the start of every step;
-//   k_sample_bits  one warp per (ray, 32-step chunk): lane j tests step
-//                  32c+j against the bitfield; the ballot is the chunk's
-//                  bit word, its popcount is added to the ray's count;
+//                  recurrence, writing t at the start of every 32-step chunk;
+//   k_sample_bits  one warp per ray, lane c walks the 32 steps of chunk c
+//                  from its stored start, testing each midpoint against the
+//                  bitfield, then stores t of every kept step in the ray's
+//                  kept list (in step order) and the ray's count;
 //   k_sample_scan  ordered exclusive scans of counts and active flags with
 //                  the capacity cut;
 //   k_sample_write one warp per kept ray: samples at their final offsets,
-//                  one sample per lane (chunk from a warp scan of the
-//                  bit-word counts, step from the set bit of its rank), then
-//                  the ray record with its ground-truth colour.
+//                  one sample per lane from the kept list, then the ray
+//                  record with its ground-truth colour.
 // All float arithmetic that decides which steps are kept uses explicit
 // rounding intrinsics, so the CPU oracle reproduces per-ray counts and
 // offsets bit for bit.  (The reference normalises with the approximate
@@ -54,24 +54,17 @@ __device__ __forceinline__ uint32_t* counts_of(const SamplerArgs& a, uint32_t fr
 }
 
 // Step recurrence of one ray per thread (reference backend-cuda.cu:455-468).
-// The chain is serial by definition; t of every step is stored so that the
-// bitfield tests and the sample writes run one lane per step.  Blocks are a
-// single warp, so the few warps of a step spread over the SMs.  Each lane
-// stages 32 steps in shared memory; while the next 32 steps run, the warp
-// writes the staged block out as 128-byte rows of the [ray][step] array, one
-// row per step, filling the latency of the recurrence.
+// The chain is serial by definition and is the whole cost of this kernel, so
+// nothing else sits in its loop: it stores only t at the start of every
+// 32-step chunk, and the bitfield tests and the sample writes re-run at most
+// 31 steps of the same rounded recurrence from there (step_t), which gives
+// the same t bit for bit.  Blocks are a single warp, so the few warps of a
+// step spread over the SMs.
 constexpr uint32_t kMarchBlock = 32;
-
-__device__ __forceinline__ void march_flush_row(const SamplerArgs& a, const float* stage, uint32_t r0, uint32_t k,
-                                                uint32_t base, uint32_t steps_k, uint32_t lane) {
-    if (base + lane < steps_k)
-        a.steps_t[static_cast<unsigned long long>(r0 + k) * a.tc.max_steps + base + lane] = stage[k * 33u + lane];
-}
 
 __global__ void __launch_bounds__(kMarchBlock) k_march(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     __shared__ float cam[16];
-    __shared__ float stage[2][32 * 33];
     const uint32_t frame = a.state->frame_index;
     const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
     const uint32_t r0 = blockIdx.x * kMarchBlock;
@@ -80,43 +73,31 @@ __global__ void __launch_bounds__(kMarchBlock) k_march(const SamplerArgs a) {
     if (lane < 12u) cam[lane] = a.cams[16ull * train_camera(frame, tc.n_images) + lane];
     __syncwarp();
     const uint32_t r = r0 + lane;
+    if (r >= n_rays) return;
     const AabbConsts box = aabb_of(tc);
     Ray ray{};
     RayGeom g{};
-    bool live = r < n_rays && make_ray(tc, box, cam, ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r), ray, g.px, g.py);
+    bool live = make_ray(tc, box, cam, ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r), ray, g.px, g.py);
     const float dt_min = live ? __fdiv_rn(__fsub_rn(ray.tf, ray.tn), static_cast<float>(tc.max_steps)) : 0.0f;
     // Below tf every dt is positive, and once t reaches tf it never drops
     // below it again (past tf, dt = tf - t is exact and brings t back to tf),
     // so the steps with t < tf are a prefix: 32 steps run without a per-step
     // exit test and are counted after.
+    float* chunks = a.chunk_t + static_cast<unsigned long long>(r) * tc.mask_words;
     float t = ray.tn;
-    uint32_t i = 0u, i_prev = 0u, blk = 0u;
-    for (uint32_t base = 0; __any_sync(0xffffffffu, live); base += 32u, ++blk) {
-        float* mine = stage[blk & 1u] + lane * 33u;
-        const float* prev = stage[(blk & 1u) ^ 1u];
+    uint32_t i = 0u;
+    for (uint32_t base = 0; live; base += 32u) {
+        chunks[base >> 5] = t;
         uint32_t nv = 0u;
-#pragma unroll 8
+#pragma unroll
         for (uint32_t j = 0; j < 32u; ++j) {
-            mine[j] = t;
             nv += t < ray.tf ? 1u : 0u;
             t = __fadd_rn(t, march_dt(t, ray.tf, dt_min, tc.cone));
-            const uint32_t steps_j = __shfl_sync(0xffffffffu, i_prev, j);
-            if (base != 0u) march_flush_row(a, prev, r0, j, base - 32u, steps_j, lane);
         }
-        if (live) {
-            nv = min(nv, tc.max_steps - base);
-            i = base + nv;
-            live = nv == 32u && i < tc.max_steps;
-        }
-        i_prev = i;
-        __syncwarp();
-        if (!__any_sync(0xffffffffu, live)) {  // last block: flush it now
-#pragma unroll 8
-            for (uint32_t k = 0; k < 32u; ++k) march_flush_row(a, mine - lane * 33u, r0, k, base, __shfl_sync(0xffffffffu, i, k), lane);
-        }
+        nv = min(nv, tc.max_steps - base);
+        i = base + nv;
+        live = nv == 32u && i < tc.max_steps;
     }
-    if (r >= n_rays) return;
-    counts_of(a, frame)[r] = 0u;
     g.tf = ray.tf;
     g.dt_min = dt_min;
     g.n_steps = i;
@@ -128,44 +109,62 @@ __global__ void __launch_bounds__(kMarchBlock) k_march(const SamplerArgs a) {
     a.geom[r] = g;
 }
 
-// Midpoint position and dt of step i of a ray.
-__device__ __forceinline__ float step_point(const SamplerArgs& a, const RayGeom& g, uint32_t r, uint32_t i, float p[3]) {
-    const float t = a.steps_t[static_cast<unsigned long long>(r) * a.tc.max_steps + i];
-    const float dt = march_dt(t, g.tf, g.dt_min, a.tc.cone);
-    const float mid = march_mid(t, dt);
-#pragma unroll
-    for (int k = 0; k < 3; ++k) p[k] = __fmaf_rn(mid, g.d[k], g.o[k]);
-    return dt;
-}
-
 __device__ __forceinline__ uint32_t warps_in_grid() { return gridDim.x * (blockDim.x / 32u); }
 __device__ __forceinline__ uint32_t warp_in_grid() { return blockIdx.x * (blockDim.x / 32u) + (threadIdx.x >> 5); }
 
-// Bitfield tests: a grid-stride loop over (ray, chunk) pairs, one warp each.
+// Bitfield tests: a grid-stride loop over rays, one warp each.  Lane c takes
+// chunk c (32 consecutive steps): from the chunk's stored start it runs the
+// march's own rounded recurrence, so every t is the march's bit for bit, and
+// tests each step's midpoint against the bitfield.  A warp scan of the
+// chunks' kept counts places each lane's kept steps in the ray's kept list
+// ([ray][max_steps], step order), which a second walk of the chunk fills
+// with their t.  The ray's sample count is the warp's total.
 __global__ void __launch_bounds__(kSamplerBlock) k_sample_bits(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
     uint32_t* counts = counts_of(a, a.state->frame_index);
     const uint32_t lane = threadIdx.x & 31u;
     const AabbConsts box = aabb_of(tc);
-    const unsigned long long total = static_cast<unsigned long long>(n_rays) * tc.mask_words;
-    for (unsigned long long w = warp_in_grid(); w < total; w += warps_in_grid()) {
-        const uint32_t r = static_cast<uint32_t>(w / tc.mask_words), c = static_cast<uint32_t>(w % tc.mask_words);
-        const RayGeom& g = a.geom[r];
-        const uint32_t n_steps = g.n_steps;
-        if (32u * c >= n_steps) continue;
-        const uint32_t i = 32u * c + lane;
-        bool occ = false;
-        if (i < n_steps) {
-            float p[3];
-            step_point(a, g, r, i, p);
-            occ = occupied(a.bitfield, tc.grid_res, box, p);
+    for (uint32_t r = warp_in_grid(); r < n_rays; r += warps_in_grid()) {
+        const RayGeom g = a.geom[r];
+        const float* ct = a.chunk_t + static_cast<unsigned long long>(r) * tc.mask_words;
+        float* kt = a.kept_t + static_cast<unsigned long long>(r) * tc.max_steps;
+        uint32_t kept = 0u;
+        for (uint32_t c0 = 0; 32u * c0 < g.n_steps; c0 += 32u) {
+            const uint32_t first = 32u * (c0 + lane);
+            const uint32_t m = first < g.n_steps ? min(32u, g.n_steps - first) : 0u;
+            const float t0 = m ? ct[c0 + lane] : 0.0f;
+            uint32_t bits = 0u;
+            float t = t0;
+#pragma unroll 8
+            for (uint32_t j = 0; j < 32u; ++j) {
+                const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
+                if (j < m) {
+                    const float mid = march_mid(t, dt);
+                    const float p[3] = {__fmaf_rn(mid, g.d[0], g.o[0]), __fmaf_rn(mid, g.d[1], g.o[1]),
+                                        __fmaf_rn(mid, g.d[2], g.o[2])};
+                    if (occupied(a.bitfield, tc.grid_res, box, p)) bits |= 1u << j;
+                }
+                t = __fadd_rn(t, dt);
+            }
+            const uint32_t cnt = static_cast<uint32_t>(__popc(bits));
+            uint32_t incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= static_cast<uint32_t>(o)) incl += x;
+            }
+            uint32_t out = kept + incl - cnt;
+            t = t0;
+            for (uint32_t left = bits; left; ) {
+                const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
+                if (left & 1u) kt[out++] = t;
+                left >>= 1;
+                t = __fadd_rn(t, dt);
+            }
+            kept += __shfl_sync(0xffffffffu, incl, 31);
         }
-        const uint32_t bits = __ballot_sync(0xffffffffu, occ);
-        if (lane == 0u) {
-            a.masks[static_cast<unsigned long long>(r) * tc.mask_words + c] = bits;
-            if (bits) atomicAdd(counts + r, static_cast<uint32_t>(__popc(bits)));
-        }
+        if (lane == 0u) counts[r] = kept;
     }
 }
 
@@ -298,30 +297,9 @@ __device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom
     a.rays[slot] = rec;
 }
 
-// Position of the set bit of rank `rank` (0-based, from bit 0) in `bits`,
-// which has more than `rank` set bits: a binary search over bit positions
-// with population counts of the lower half of the remaining window.
-__device__ __forceinline__ uint32_t select_bit(uint32_t bits, uint32_t rank) {
-    uint32_t pos = 0u;
-#pragma unroll
-    for (uint32_t w = 16u; w > 0u; w >>= 1) {
-        const uint32_t low = static_cast<uint32_t>(__popc(bits & ((1u << w) - 1u)));
-        if (rank >= low) {
-            rank -= low;
-            bits >>= w;
-            pos += w;
-        }
-    }
-    return pos;
-}
-
-// One warp per kept ray (grid-stride).  Lane k holds the bit word of chunk
-// 32q+k and a warp scan gives the chunks' inclusive sample counts.  Then each
-// lane writes one sample at a time: sample s of the group lies in the first
-// chunk whose inclusive count exceeds s (binary search over the 32 counts
-// with shuffles) at the set bit of rank s - (samples of the earlier chunks).
-// Consecutive lanes write consecutive samples, and each round's step loads
-// are independent, so a ray costs one memory round trip per 32 samples.
+// One warp per kept ray (grid-stride): lane k writes samples k, k+32, ...
+// of the ray at their final offsets, each from its t in the ray's kept list
+// (midpoint position and dt as the march defines them).
 __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     const uint32_t frame = a.state->frame_index;
@@ -336,37 +314,14 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
         if (slot == 0xFFFFFFFFu) continue;
         const uint32_t excl = a.ray_offset[r];
         const RayGeom& g = a.geom[r];
-        const uint32_t* rm = a.masks + static_cast<unsigned long long>(r) * tc.mask_words;
-        const uint32_t n_chunks = (g.n_steps + 31u) / 32u;
-        uint32_t out = excl;
-        for (uint32_t c0 = 0; c0 < n_chunks; c0 += 32u) {
-            const uint32_t mine = c0 + lane < n_chunks ? rm[c0 + lane] : 0u;
-            const uint32_t cnt = __popc(mine);
-            uint32_t incl = cnt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= static_cast<uint32_t>(o)) incl += x;
-            }
-            const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-            for (uint32_t sb = 0; sb < total; sb += 32u) {
-                const uint32_t si = sb + lane;
-                uint32_t k = 0u;  // chunks whose inclusive count is <= si (at most 31)
-#pragma unroll
-                for (uint32_t step = 16u; step > 0u; step >>= 1) {
-                    const uint32_t v = __shfl_sync(0xffffffffu, incl, k + step - 1u);
-                    if (v <= si) k += step;
-                }
-                const uint32_t bits = __shfl_sync(0xffffffffu, mine, k);
-                const uint32_t first = __shfl_sync(0xffffffffu, incl, k) - static_cast<uint32_t>(__popc(bits));
-                if (si < total) {
-                    float p[3];
-                    const float dt = step_point(a, g, r, 32u * (c0 + k) + select_bit(bits, si - first), p);
-                    a.pos_dt[out + si] = make_float4(p[0], p[1], p[2], dt);
-                    a.sample_ray[out + si] = slot;
-                }
-            }
-            out += total;
+        const float* kt = a.kept_t + static_cast<unsigned long long>(r) * tc.max_steps;
+        for (uint32_t si = lane; si < count; si += 32u) {
+            const float t = kt[si];
+            const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
+            const float mid = march_mid(t, dt);
+            a.pos_dt[excl + si] = make_float4(__fmaf_rn(mid, g.d[0], g.o[0]), __fmaf_rn(mid, g.d[1], g.o[1]),
+                                              __fmaf_rn(mid, g.d[2], g.o[2]), dt);
+            a.sample_ray[excl + si] = slot;
         }
         if (lane == 0u) write_record(a, g, r, slot, excl, count, frame, camera);
     }
