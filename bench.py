@@ -247,7 +247,7 @@ def run_ours(args):
     stats = ctx.stats()
 
     # Kernel-by-kernel timing of the same step (events between launches).
-    prof = np.zeros(10)
+    prof = np.zeros(len(abi.STEP_KERNELS))
     n_prof = args.profile_steps
     prof_samples = 0
     for _ in range(n_prof):
@@ -319,7 +319,7 @@ def run_ours(args):
 
 
 def kernel_table(ctx, prof_ms, samples):
-    """Algorithmic bytes per launch for each step kernel (DESIGN.md lists the per-unit figures)."""
+    """Algorithmic bytes per launch for each step kernel (the per-unit figures are in the comments below)."""
     from nerf_b200 import abi
     n_params = ctx.n_params
     n_grid = ctx.n_grid
@@ -336,7 +336,10 @@ def kernel_table(ctx, prof_ms, samples):
         "grad_stats": n_grid * 2 + (n_params - n_grid) * 4,
         "wgrad_reduce": (ctx_partials(ctx) + 1) * 10240 * 4,
         "occupancy_update": cells * 8 + cells // 8,
-        "sampler": samples * (16 + 4) * 1,
+        # t of every kept step written to the ray's kept list
+        "sample_bits": samples * 4,
+        # kept t read, pos/dt 16 + ray id 4 written
+        "sample_write": samples * (4 + 16 + 4),
         "occupancy_query": 0,
         "allreduce": n_grid * 2 + 10248 * 4,
     }

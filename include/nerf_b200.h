@@ -72,11 +72,11 @@ NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out
 NERF_API NerfStatus nerf_b200_context_stream(void* context, void** stream);
 /* One training step launched kernel by kernel instead of as the captured
  * graph, with CUDA events between launches.  Segments: occupancy query,
- * occupancy update, sampler (bitfield tests, compaction scan, sample
- * writes), field forward, composite, field backward, weight-gradient
- * reduce (folded into the statistics on one GPU), gradient exchange (0 on
- * one GPU), gradient statistics, Adam (with the next step's ray march). */
-#define NERF_B200_STEP_KERNELS 10
+ * occupancy update, sampler bitfield tests, compaction scan, sample writes,
+ * field forward, composite, field backward, weight-gradient reduce (folded
+ * into the statistics on one GPU), gradient exchange (0 on one GPU),
+ * gradient statistics, the next step's ray march, Adam. */
+#define NERF_B200_STEP_KERNELS 13
 typedef struct NerfB200StepProfile {
     float milliseconds[NERF_B200_STEP_KERNELS];
     float total_milliseconds;

@@ -207,12 +207,12 @@ class NerfB200RenderInfo(C.Structure):
     _fields_ = [("rays", C.c_uint64), ("samples", C.c_uint64), ("milliseconds", C.c_float)]
 
 
-STEP_KERNELS = ["occupancy_query", "occupancy_update", "sampler", "field_forward", "composite", "field_backward",
-                "wgrad_reduce", "allreduce", "grad_stats", "adam"]
+STEP_KERNELS = ["occupancy_query", "occupancy_update", "sample_bits", "sample_scan", "sample_write", "field_forward",
+                "composite", "field_backward", "wgrad_reduce", "allreduce", "grad_stats", "march", "adam"]
 
 
 class NerfB200StepProfile(C.Structure):
-    _fields_ = [("milliseconds", C.c_float * 10), ("total_milliseconds", C.c_float)]
+    _fields_ = [("milliseconds", C.c_float * len(STEP_KERNELS)), ("total_milliseconds", C.c_float)]
 
 
 class NerfB200SceneDesc(C.Structure):

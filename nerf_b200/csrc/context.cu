@@ -47,7 +47,7 @@ static_assert(sizeof(NerfB200RayRecord) == sizeof(RayRecord), "ray record mirror
 static_assert(sizeof(StatsBlock) == sizeof(NerfTrainStats), "stats mirror");
 
 constexpr uint32_t kMaxStepsPerRay = 4096;  // the reference allows 256
-constexpr int kStepKernels = 10;            // timed segments of one training step
+constexpr int kStepKernels = 13;            // timed segments of one training step
 
 // ---------------------------------------------------------------- helpers
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1u) / a * a; }
@@ -686,7 +686,9 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = mark()) != cudaSuccess) return e;
     if ((e = launch_field_forward(occq, kFieldOccupancy, fwd_blocks, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if ((e = launch_occupancy_update(oa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if ((e = launch_sampler(sa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    if ((e = launch_sample_bits(sa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    if ((e = launch_sample_scan(sa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
+    if ((e = launch_sample_write(sa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     if (mlp_tc) {  // encode + SH into the training rows, then the MLPs on tcgen05
         if ((e = launch_field_encode(fa, s)) != cudaSuccess ||
             (e = launch_mlp_forward_tc_train(p16 + n_grid, feat, &state->n_samples, reinterpret_cast<float*>(raw), &state->mlp_error,
@@ -731,7 +733,8 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     // the next step's march.  (Run beside Adam on a second stream it gained
     // nothing: with HBM saturated by Adam the march's stores stall, and the
     // pair took longer than the two in order.)
-    if ((e = launch_march(sa, s)) != cudaSuccess || (e = launch_adam(op, s)) != cudaSuccess) return e;
+    if ((e = launch_march(sa, s)) != cudaSuccess || (e = mark()) != cudaSuccess || (e = launch_adam(op, s)) != cudaSuccess)
+        return e;
     // Peer mode: every rank wrote its owned fp16 parameters into every rank's
     // mirror; no rank reads them before all writes are done.
     if (comm && dp_peer && (e = launch_dp_barrier(op.dp, s)) != cudaSuccess) return e;

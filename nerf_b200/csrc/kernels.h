@@ -125,7 +125,11 @@ constexpr uint32_t kSamplerBlock = 256;
 // step's march only depends on the frame and the ray count, so the training
 // step ends with the next step's march.
 cudaError_t launch_march(const SamplerArgs& a, cudaStream_t s);
-// Bitfield tests, compaction scan and sample writes (after launch_march).
+// Bitfield tests, compaction scan and sample writes (after launch_march),
+// one launch each or all three in order.
+cudaError_t launch_sample_bits(const SamplerArgs& a, cudaStream_t s);
+cudaError_t launch_sample_scan(const SamplerArgs& a, cudaStream_t s);
+cudaError_t launch_sample_write(const SamplerArgs& a, cudaStream_t s);
 cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s);
 
 // ---- compositing + loss ----

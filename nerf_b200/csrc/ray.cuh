@@ -101,9 +101,11 @@ NB_DEV bool clip_aabb(const AabbConsts& b, Ray& r) {
     return __fsub_rn(tf, tn) > 0.0f;
 }
 
-// Occupancy bit of the cell holding p (reference backend-cuda.cu:338-351),
-// in the R^3 grid of p's cascade (bitfield: cascade after cascade).
-NB_DEV bool occupied(const uint32_t* __restrict__ bits, uint32_t R, const AabbConsts& b, const float p[3]) {
+// Index of the occupancy cell holding p (reference backend-cuda.cu:338-351)
+// in the bitfield (the R^3 grids of the cascades, one after another), or
+// kNoCell when p lies outside every cascade.
+constexpr uint32_t kNoCell = 0xFFFFFFFFu;
+NB_DEV uint32_t occupancy_cell(uint32_t R, const AabbConsts& b, const float p[3]) {
     float rel[3];
     uint32_t mip = 0u;
     if (b.cascades <= 1u) {
@@ -111,7 +113,7 @@ NB_DEV bool occupied(const uint32_t* __restrict__ bits, uint32_t R, const AabbCo
         for (int k = 0; k < 3; ++k) rel[k] = __fdiv_rn(__fsub_rn(p[k], b.mn[k]), b.size[k]);
     } else {
         mip = cascade_of(b, p);
-        if (mip >= b.cascades) return false;
+        if (mip >= b.cascades) return kNoCell;
         const float s = pow2f(mip);
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
@@ -119,13 +121,21 @@ NB_DEV bool occupied(const uint32_t* __restrict__ bits, uint32_t R, const AabbCo
             rel[k] = __fdiv_rn(__fsub_rn(p[k], lo), __fmul_rn(b.bsize[k], s));
         }
     }
-    if (rel[0] < 0.0f || rel[0] >= 1.0f || rel[1] < 0.0f || rel[1] >= 1.0f || rel[2] < 0.0f || rel[2] >= 1.0f) return false;
+    if (rel[0] < 0.0f || rel[0] >= 1.0f || rel[1] < 0.0f || rel[1] >= 1.0f || rel[2] < 0.0f || rel[2] >= 1.0f) return kNoCell;
     const float Rf = static_cast<float>(R);
     const uint32_t ix = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[0], Rf)));
     const uint32_t iy = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[1], Rf)));
     const uint32_t iz = min(R - 1u, static_cast<uint32_t>(__fmul_rn(rel[2], Rf)));
-    const uint32_t idx = mip * R * R * R + ix + iy * R + iz * R * R;
-    return ((__ldg(bits + (idx >> 5)) >> (idx & 31u)) & 1u) != 0u;
+    return mip * R * R * R + ix + iy * R + iz * R * R;
+}
+
+NB_DEV bool cell_bit(const uint32_t* __restrict__ bits, uint32_t cell) {
+    return cell != kNoCell && ((__ldg(bits + (cell >> 5)) >> (cell & 31u)) & 1u) != 0u;
+}
+
+// Occupancy bit of the cell holding p.
+NB_DEV bool occupied(const uint32_t* __restrict__ bits, uint32_t R, const AabbConsts& b, const float p[3]) {
+    return cell_bit(bits, occupancy_cell(R, b, p));
 }
 
 // One step of the cone-angle march (reference backend-cuda.cu:455-468):

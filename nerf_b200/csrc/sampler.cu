@@ -134,18 +134,23 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_bits(const SamplerArgs
             const uint32_t first = 32u * (c0 + lane);
             const uint32_t m = first < g.n_steps ? min(32u, g.n_steps - first) : 0u;
             const float t0 = m ? ct[c0 + lane] : 0.0f;
+            // Eight cell indices at a time, then their eight bitfield loads
+            // in flight together.
             uint32_t bits = 0u;
             float t = t0;
-#pragma unroll 8
-            for (uint32_t j = 0; j < 32u; ++j) {
-                const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
-                if (j < m) {
+            for (uint32_t j0 = 0; j0 < m; j0 += 8u) {
+                uint32_t cell[8];
+#pragma unroll
+                for (uint32_t j = 0; j < 8u; ++j) {
+                    const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
                     const float mid = march_mid(t, dt);
                     const float p[3] = {__fmaf_rn(mid, g.d[0], g.o[0]), __fmaf_rn(mid, g.d[1], g.o[1]),
                                         __fmaf_rn(mid, g.d[2], g.o[2])};
-                    if (occupied(a.bitfield, tc.grid_res, box, p)) bits |= 1u << j;
+                    cell[j] = j0 + j < m ? occupancy_cell(tc.grid_res, box, p) : kNoCell;
+                    t = __fadd_rn(t, dt);
                 }
-                t = __fadd_rn(t, dt);
+#pragma unroll
+                for (uint32_t j = 0; j < 8u; ++j) bits |= cell_bit(a.bitfield, cell[j]) ? 1u << (j0 + j) : 0u;
             }
             const uint32_t cnt = static_cast<uint32_t>(__popc(bits));
             uint32_t incl = cnt;
@@ -334,18 +339,43 @@ cudaError_t launch_march(const SamplerArgs& a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
-cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s) {
+namespace {
+cudaError_t warp_blocks(uint32_t* blocks) {  // grid-stride kernels: 8 blocks per SM
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    const uint32_t warp_blocks = static_cast<uint32_t>(sms) * 8u;  // grid-stride kernels: 8 blocks per SM
-    k_sample_bits<<<warp_blocks, kSamplerBlock, 0, s>>>(a);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_sample_scan<<<1, kScanThreads, 0, s>>>(a);
-    if ((e = cudaGetLastError()) != cudaSuccess) return e;
-    k_sample_write<<<warp_blocks, kSamplerBlock, 0, s>>>(a);
+    *blocks = static_cast<uint32_t>(sms) * 8u;
+    return cudaSuccess;
+}
+}  // namespace
+
+cudaError_t launch_sample_bits(const SamplerArgs& a, cudaStream_t s) {
+    uint32_t blocks = 0;
+    cudaError_t e = warp_blocks(&blocks);
+    if (e != cudaSuccess) return e;
+    k_sample_bits<<<blocks, kSamplerBlock, 0, s>>>(a);
     return cudaGetLastError();
+}
+
+cudaError_t launch_sample_scan(const SamplerArgs& a, cudaStream_t s) {
+    k_sample_scan<<<1, kScanThreads, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sample_write(const SamplerArgs& a, cudaStream_t s) {
+    uint32_t blocks = 0;
+    cudaError_t e = warp_blocks(&blocks);
+    if (e != cudaSuccess) return e;
+    k_sample_write<<<blocks, kSamplerBlock, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sampler(const SamplerArgs& a, cudaStream_t s) {
+    cudaError_t e = launch_sample_bits(a, s);
+    if (e == cudaSuccess) e = launch_sample_scan(a, s);
+    if (e == cudaSuccess) e = launch_sample_write(a, s);
+    return e;
 }
 
 }  // namespace nb
