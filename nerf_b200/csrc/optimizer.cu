@@ -20,29 +20,47 @@
 namespace nb {
 namespace {
 
-// Sum over c = 0..n-1 of partials[c][i], added in order of c.  The loads of
-// 32 partials are issued before their adds, so a thread waits for one
-// memory round trip per 32 partials instead of one per partial (the order of
-// the additions, and so the result, is that of the plain loop).
-__device__ __forceinline__ float sum_partials(const float* __restrict__ partials, uint32_t n, uint32_t i) {
-    const float* p = partials + i;
+// Weight gradients from the backward's per-CTA partials ([c][kMlpParams]):
+// a 256-thread block sums the partials of 32 consecutive parameters (one per
+// lane).  Warp w adds rows c of the w-th eighth of the partials in order,
+// reading one 128-byte line per row, with 32 rows' loads issued before their
+// adds; the eight warp sums are then added in warp order.  Every block takes
+// one memory round trip per 32 rows of its eighth, and the fixed order makes
+// the result deterministic.  Returns the sum in warp 0 (lane = parameter).
+constexpr uint32_t kWgradParamsPerBlock = 32;
+constexpr uint32_t kWgradBlocks = kMlpParams / kWgradParamsPerBlock;
+static_assert(kMlpParams % kWgradParamsPerBlock == 0, "whole blocks of weight gradients");
+
+__device__ __forceinline__ float wgrad_block_sum(const float* __restrict__ partials, uint32_t n, uint32_t block) {
+    __shared__ float ws[8][32];
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t per = (n + 7u) / 8u;
+    const uint32_t c0 = min(n, warp * per), c1 = min(n, c0 + per);
+    const float* p = partials + block * kWgradParamsPerBlock + lane;
     float s = 0.0f;
-    uint32_t c = 0;
-    for (; c + 32u <= n; c += 32u) {
+    uint32_t c = c0;
+    for (; c + 32u <= c1; c += 32u) {
         float v[32];
 #pragma unroll
         for (uint32_t k = 0; k < 32u; ++k) v[k] = __ldcs(p + static_cast<unsigned long long>(c + k) * kMlpParams);
 #pragma unroll
         for (uint32_t k = 0; k < 32u; ++k) s += v[k];
     }
-    for (; c < n; ++c) s += __ldcs(p + static_cast<unsigned long long>(c) * kMlpParams);
-    return s;
+    for (; c < c1; ++c) s += __ldcs(p + static_cast<unsigned long long>(c) * kMlpParams);
+    ws[warp][lane] = s;
+    __syncthreads();
+    float g = 0.0f;
+    if (warp == 0u) {
+        g = ws[0][lane];
+#pragma unroll
+        for (uint32_t w = 1; w < 8u; ++w) g += ws[w][lane];
+    }
+    return g;
 }
 
 __global__ void __launch_bounds__(256) k_wgrad_reduce(const float* __restrict__ partials, uint32_t n_partials, float* mlp_grad) {
-    const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= kMlpParams) return;
-    mlp_grad[i] = sum_partials(partials, n_partials, i);
+    const float g = wgrad_block_sum(partials, n_partials, blockIdx.x);
+    if (threadIdx.x < 32u) mlp_grad[blockIdx.x * kWgradParamsPerBlock + threadIdx.x] = g;
 }
 
 __device__ __forceinline__ void adam_scalars(const TrainConsts& tc, float grad_norm, uint32_t nonfinite, uint32_t step,
@@ -63,8 +81,6 @@ __device__ __forceinline__ void adam_scalars(const TrainConsts& tc, float grad_n
     o.skip_update = skip ? 1u : 0u;
 }
 
-constexpr uint32_t kWgradBlocks = (kMlpParams + 255u) / 256u;
-
 __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     uint64_t n_chunks = a.n_params / 8u;
     const uint64_t grid_chunks = a.n_grid / 8u;
@@ -80,10 +96,9 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
         // (fixed order) and take the MLP part of the statistics; the others
         // take the hash-table part.
         if (blockIdx.x < kWgradBlocks) {
-            const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-            if (i < kMlpParams) {
-                const float g = sum_partials(a.partials, a.n_partials, i);
-                a.mlp_grad[i] = g;
+            const float g = wgrad_block_sum(a.partials, a.n_partials, blockIdx.x);
+            if (threadIdx.x < 32u) {
+                a.mlp_grad[blockIdx.x * kWgradParamsPerBlock + threadIdx.x] = g;
                 if (!isfinite(g)) bad = 1u;
                 else sum = g * g;
             }
@@ -440,7 +455,7 @@ uint32_t grad_stats_blocks(uint64_t n_params) {
 }
 
 cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s) {
-    k_wgrad_reduce<<<(kMlpParams + 255u) / 256u, 256, 0, s>>>(a.partials, a.n_partials, a.mlp_grad);
+    k_wgrad_reduce<<<kWgradBlocks, 256, 0, s>>>(a.partials, a.n_partials, a.mlp_grad);
     return cudaGetLastError();
 }
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s) {

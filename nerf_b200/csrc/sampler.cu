@@ -248,14 +248,38 @@ __global__ void __launch_bounds__(kScanThreads) k_sample_scan(const SamplerArgs 
     }
 }
 
+// Bilinear footprint of a ray's ground-truth fetch at the unflipped pixel
+// position (reference backend-cuda.cu:471-499): texel k (k = 0..3) is
+// (x0 or x1 for bit 0 of k, y0 or y1 for bit 1).
+struct Footprint {
+    unsigned long long texel[4];
+    float tx, ty;
+};
+
+__device__ __forceinline__ Footprint footprint(const TrainConsts& tc, const RayGeom& g, uint32_t camera) {
+    const float pxc = fmaxf(0.0f, fminf(g.px, __fsub_rn(static_cast<float>(tc.width), 1.0f)));
+    const float pyc = fmaxf(0.0f, fminf(g.py, __fsub_rn(static_cast<float>(tc.height), 1.0f)));
+    const int x0 = static_cast<int>(floorf(pxc)), y0 = static_cast<int>(floorf(pyc));
+    const int x1 = min(x0 + 1, static_cast<int>(tc.width) - 1), y1 = min(y0 + 1, static_cast<int>(tc.height) - 1);
+    const unsigned long long base = static_cast<unsigned long long>(camera) * tc.width * tc.height;
+    Footprint f;
+    f.texel[0] = base + static_cast<uint32_t>(y0) * tc.width + x0;
+    f.texel[1] = base + static_cast<uint32_t>(y0) * tc.width + x1;
+    f.texel[2] = base + static_cast<uint32_t>(y1) * tc.width + x0;
+    f.texel[3] = base + static_cast<uint32_t>(y1) * tc.width + x1;
+    f.tx = __fsub_rn(pxc, static_cast<float>(x0));
+    f.ty = __fsub_rn(pyc, static_cast<float>(y0));
+    return f;
+}
+
 // Ray record of a kept ray: direction, sample range, background and the
-// ground truth -- a bilinear RGBA8 fetch at the unflipped pixel position,
-// composited on the ray's background (reference backend-cuda.cu:471-499).
+// ground truth -- the bilinear blend of the footprint's texels q00, q10, q01,
+// q11, composited on the ray's background.
 __device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom& g, uint32_t r, uint32_t slot, uint32_t excl,
-                                             uint32_t count, uint32_t frame, uint32_t camera) {
+                                             uint32_t count, uint32_t frame, const Footprint& f, uint32_t q00, uint32_t q10,
+                                             uint32_t q01, uint32_t q11) {
     const TrainConsts& tc = a.tc;
     const uint32_t seed = ray_seed(frame, tc.dp_rank * tc.rays_per_batch + r);
-    const float rpx = g.px, rpy = g.py;
     a.ray_index[slot] = r;
     float bg[3] = {1.0f, 1.0f, 1.0f};
     if (tc.background == 1u) {
@@ -263,16 +287,7 @@ __device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom
         bg[1] = rand01(seed ^ kBgSalt1);
         bg[2] = rand01(seed ^ kBgSalt2);
     }
-    const float pxc = fmaxf(0.0f, fminf(rpx, __fsub_rn(static_cast<float>(tc.width), 1.0f)));
-    const float pyc = fmaxf(0.0f, fminf(rpy, __fsub_rn(static_cast<float>(tc.height), 1.0f)));
-    const int x0 = static_cast<int>(floorf(pxc)), y0 = static_cast<int>(floorf(pyc));
-    const int x1 = min(x0 + 1, static_cast<int>(tc.width) - 1), y1 = min(y0 + 1, static_cast<int>(tc.height) - 1);
-    const float tx = __fsub_rn(pxc, static_cast<float>(x0)), ty = __fsub_rn(pyc, static_cast<float>(y0));
-    const uint32_t* img = reinterpret_cast<const uint32_t*>(a.images) + static_cast<unsigned long long>(camera) * tc.width * tc.height;
-    const uint32_t q00 = __ldg(img + static_cast<uint32_t>(y0) * tc.width + x0);
-    const uint32_t q10 = __ldg(img + static_cast<uint32_t>(y0) * tc.width + x1);
-    const uint32_t q01 = __ldg(img + static_cast<uint32_t>(y1) * tc.width + x0);
-    const uint32_t q11 = __ldg(img + static_cast<uint32_t>(y1) * tc.width + x1);
+    const float tx = f.tx, ty = f.ty;
     const float inv255 = 1.0f / 255.0f;
     const float omtx = __fsub_rn(1.0f, tx), omty = __fsub_rn(1.0f, ty);
     float v[4];
@@ -313,13 +328,15 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
     const uint32_t lane = threadIdx.x & 31u;
     const uint32_t* counts = counts_of(a, frame);
     for (uint32_t r = warp_in_grid(); r < n_rays; r += warps_in_grid()) {
-        const uint32_t count = counts[r];
-        if (count == 0u) continue;
-        const uint32_t slot = a.ray_slot[r];
-        if (slot == 0xFFFFFFFFu) continue;
-        const uint32_t excl = a.ray_offset[r];
-        const RayGeom& g = a.geom[r];
+        const uint32_t count = counts[r], slot = a.ray_slot[r], excl = a.ray_offset[r];
+        if (count == 0u || slot == 0xFFFFFFFFu) continue;
+        const RayGeom g = a.geom[r];
+        // Lanes 0-3 fetch the record's four texels before the samples.
+        const Footprint f = footprint(tc, g, camera);
+        const unsigned long long ti = (lane & 2u) ? ((lane & 1u) ? f.texel[3] : f.texel[2]) : ((lane & 1u) ? f.texel[1] : f.texel[0]);
+        const uint32_t texel = lane < 4u ? __ldg(reinterpret_cast<const uint32_t*>(a.images) + ti) : 0u;
         const float* kt = a.kept_t + static_cast<unsigned long long>(r) * tc.max_steps;
+#pragma unroll 4
         for (uint32_t si = lane; si < count; si += 32u) {
             const float t = kt[si];
             const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
@@ -328,7 +345,9 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
                                               __fmaf_rn(mid, g.d[2], g.o[2]), dt);
             a.sample_ray[excl + si] = slot;
         }
-        if (lane == 0u) write_record(a, g, r, slot, excl, count, frame, camera);
+        const uint32_t q00 = __shfl_sync(0xffffffffu, texel, 0), q10 = __shfl_sync(0xffffffffu, texel, 1);
+        const uint32_t q01 = __shfl_sync(0xffffffffu, texel, 2), q11 = __shfl_sync(0xffffffffu, texel, 3);
+        if (lane == 0u) write_record(a, g, r, slot, excl, count, frame, f, q00, q10, q01, q11);
     }
 }
 
