@@ -53,14 +53,21 @@ __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a
         float T = 1.0f;
         float acc0 = 0.0f, acc1 = 0.0f, acc2 = 0.0f;
         uint32_t used = count;
+        // Each chunk's loads are issued one chunk ahead.
+        float4 r_next = make_float4(0.f, 0.f, 0.f, 0.f);
+        float dt_next = 0.0f;
+        if (lane < count) {
+            r_next = a.raw[b + lane];
+            dt_next = a.pos_dt[b + lane].w;
+        }
         for (uint32_t base = 0; base < count; base += 32u) {
             const uint32_t i = base + lane;
             const bool valid = i < count;
-            float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-            float dt = 0.0f;
-            if (valid) {
-                r = a.raw[b + i];
-                dt = fmaxf(0.0f, a.pos_dt[b + i].w);
+            const float4 r = r_next;
+            const float dt = fmaxf(0.0f, dt_next);
+            if (i + 32u < count) {
+                r_next = a.raw[b + i + 32u];
+                dt_next = a.pos_dt[b + i + 32u].w;
             }
             const float al = valid ? __fsub_rn(1.0f, expf(-__fmul_rn(expf(r.x), dt))) : 0.0f;
             const float om = __fsub_rn(1.0f, al);
@@ -108,15 +115,24 @@ __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a
             float s0 = __fmul_rn(T, ray.bg[0]), s1 = __fmul_rn(T, ray.bg[1]), s2 = __fmul_rn(T, ray.bg[2]);
             const float ls = a.loss_scale;
             if (used > 0u) {
-                for (int base = static_cast<int>((used - 1u) & ~31u); base >= 0; base -= 32) {
+                // Chunks from the last used one down, loads one chunk ahead.
+                const int last = static_cast<int>((used - 1u) & ~31u);
+                float4 rn = make_float4(0.f, 0.f, 0.f, 0.f);
+                float dtn = 0.0f, tn = 0.0f;
+                if (static_cast<uint32_t>(last) + lane < used) {
+                    rn = a.raw[b + last + lane];
+                    dtn = a.pos_dt[b + last + lane].w;
+                    tn = a.dout[b + last + lane].x;
+                }
+                for (int base = last; base >= 0; base -= 32) {
                     const uint32_t i = static_cast<uint32_t>(base) + lane;
                     const bool valid = i < used;
-                    float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
-                    float dt = 0.0f, trans = 0.0f;
-                    if (valid) {
-                        r = a.raw[b + i];
-                        dt = fmaxf(0.0f, a.pos_dt[b + i].w);
-                        trans = a.dout[b + i].x;
+                    const float4 r = rn;
+                    const float dt = fmaxf(0.0f, dtn), trans = tn;
+                    if (base >= 32) {  // every lane of an earlier chunk is below used
+                        rn = a.raw[b + i - 32u];
+                        dtn = a.pos_dt[b + i - 32u].w;
+                        tn = a.dout[b + i - 32u].x;
                     }
                     const float e = expf(-__fmul_rn(expf(r.x), dt));
                     const float al = __fsub_rn(1.0f, e);
