@@ -500,7 +500,9 @@ def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
                      options=options(nb))
     if world > 1:
         ctx.dp_init(rank, world, uid)
+    t_create = time.perf_counter()
     ctx.configure(train_config(nb))
+    t_configure = time.perf_counter()
     for _ in range(steps):
         ctx.train_step()
         ctx.stats()
@@ -518,6 +520,7 @@ def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
         secs, samples = float(t[0]), float(t[1])
     h2d = ds_pinned.images.nbytes + ds_pinned.cameras.nbytes
     return {"value": samples / secs, "unit": "samples/s", "steps": steps, "seconds": secs,
+            "phases_s": {"create_upload": t_create - t0, "configure": t_configure - t_create, "steps": t1 - t_configure},
             "h2d_bytes_per_step": h2d / steps, "d2h_bytes_per_step": 20,
             "note": "create+upload, configure and every step train_step + read_train_stats, wall clock, max over ranks; "
                     "includes the occupancy warm-up phase of a fresh job"}

@@ -210,6 +210,12 @@ struct Context {
     __half* grid_grad = nullptr;
     float* mlp_grad = nullptr;
     DeviceState* state = nullptr;
+    // Mapped pinned mirror of the step statistics, written by the statistics
+    // kernel; current while the last writer of the device statistics was a
+    // step (host writes of the device state make it stale).
+    StatsBlock* stats_host = nullptr;
+    StatsBlock* stats_host_dev = nullptr;
+    bool stats_host_current = false;
     float* density = nullptr;
     uint32_t* bitfield = nullptr;
     uint32_t* full_bitfield = nullptr;  // all cells occupied (render before any occupancy exists)
@@ -292,6 +298,9 @@ struct Context {
         comm = nullptr;
         if (stream) cudaStreamDestroy(stream);
         stream = nullptr;
+        if (stats_host) cudaFreeHost(stats_host);
+        stats_host = stats_host_dev = nullptr;
+        stats_host_current = false;
     }
     NerfStatus init(const NerfCreateDesc& d, const NerfB200Options& o);
     NerfStatus configure(const NerfTrainingConfig& c);
@@ -396,6 +405,10 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     if (prop.major < 10) return NERF_STATUS_FAILURE;  // built for sm_100a only
     if (ensure_attributes() != cudaSuccess) return NERF_STATUS_FAILURE;
     if (cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&stats_host), sizeof(StatsBlock), cudaHostAllocMapped) != cudaSuccess ||
+        cudaHostGetDevicePointer(reinterpret_cast<void**>(&stats_host_dev), stats_host, 0) != cudaSuccess)
+        return NERF_STATUS_FAILURE;
+    *stats_host = StatsBlock{};
     if (cudaEventCreate(&ev0) != cudaSuccess || cudaEventCreate(&ev1) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
 
     // model arena
@@ -570,6 +583,7 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     DeviceState st{};
     st.n_rays = c.rays_per_batch;
     NB_TRY(cudaMemcpyAsync(state, &st, sizeof(st), cudaMemcpyHostToDevice, stream));
+    stats_host_current = false;
     NB_TRY(cudaMemsetAsync(density, 0, static_cast<uint64_t>(words) * 32u * 4u, stream));
     NB_TRY(cudaMemsetAsync(bitfield, 0, words * 4ull, stream));
     NB_TRY(cudaMemsetAsync(m, 0, n_params * 4, stream));
@@ -710,6 +724,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = mark()) != cudaSuccess) return e;
     // One GPU: the statistics kernel also reduces the weight-gradient partials.
     op.fuse_wgrad = comm ? 0u : 1u;
+    op.stats_host = stats_host_dev;
     if (!op.fuse_wgrad && (e = launch_wgrad_reduce(op, s)) != cudaSuccess) return e;
     if ((e = mark()) != cudaSuccess) return e;
     if (comm && dp_peer) {
@@ -1140,6 +1155,7 @@ NERF_API NerfStatus nerf_train_step(void* context) {
     if (!c->configured || !c->exec) return NERF_STATUS_STATE_ERROR;
     if (cudaGraphLaunch(c->exec, c->stream) != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     ++c->host_generation;
+    c->stats_host_current = true;
     c->occupancy_valid = true;
     return NERF_STATUS_OK;
 }
@@ -1149,11 +1165,20 @@ NERF_API NerfStatus nerf_read_train_stats(void* context, NerfTrainStats* out) {
     Context* c = as_ctx(context);
     std::lock_guard<std::mutex> lk(c->mu);
     if (!c->configured) return NERF_STATUS_STATE_ERROR;
-    NB_TRY(cudaMemcpyAsync(out, &c->state->stats, sizeof(NerfTrainStats), cudaMemcpyDeviceToHost, c->stream));
+    const bool mirror = c->stats_host_current;
+    if (!mirror) NB_TRY(cudaMemcpyAsync(out, &c->state->stats, sizeof(NerfTrainStats), cudaMemcpyDeviceToHost, c->stream));
     uint32_t dp_error = 0u, mlp_error = 0u;
     if (c->dp_peer) NB_TRY(cudaMemcpyAsync(&dp_error, &c->dp_sync->error, 4, cudaMemcpyDeviceToHost, c->stream));
     if (c->mlp_tc) NB_TRY(cudaMemcpyAsync(&mlp_error, &c->state->mlp_error, 4, cudaMemcpyDeviceToHost, c->stream));
     NB_TRY(cudaStreamSynchronize(c->stream));
+    if (mirror) {
+        const volatile nb::StatsBlock* h = c->stats_host;
+        out->loss = h->loss;
+        out->grad_norm = h->grad_norm;
+        out->has_nonfinite = h->has_nonfinite;
+        out->completed_steps = h->completed_steps;
+        out->last_train_camera = h->last_train_camera;
+    }
     c->host_generation = out->completed_steps;
     // A data-parallel barrier that timed out (a rank stopped stepping): the
     // replicas are no longer in step.  A tensor-core MLP kernel whose MMAs did
@@ -1271,6 +1296,7 @@ NERF_API NerfStatus nerf_load_network_weights(void* context, const NerfCheckpoin
     nb::DeviceState st{};
     st.n_rays = c->configured ? c->cfg.rays_per_batch : 0u;
     NB_TRY(cudaMemcpyAsync(c->state, &st, sizeof(st), cudaMemcpyHostToDevice, c->stream));
+    c->stats_host_current = false;
     NB_TRY(cudaMemsetAsync(c->density, 0, static_cast<uint64_t>(c->words) * 32u * 4u, c->stream));
     NB_TRY(cudaMemsetAsync(c->bitfield, 0, c->words * 4ull, c->stream));
     if (c->configured) NB_TRY(nb::launch_march(c->sampler_args(), c->stream));  // the step state restarted at frame 0
@@ -1394,6 +1420,7 @@ NERF_API NerfStatus nerf_b200_load_training_state(void* context, const char* pat
     st.grad_sumsq = 0.0f;
     st.nonfinite = 0u;
     NB_TRY(cudaMemcpyAsync(c->state, &st, sizeof(st), cudaMemcpyHostToDevice, c->stream));
+    c->stats_host_current = false;
     NB_TRY(nb::launch_march(c->sampler_args(), c->stream));  // the next step's march (frame and ray count restored)
     NB_TRY(cudaStreamSynchronize(c->stream));
     c->occupancy_valid = true;
@@ -1599,6 +1626,7 @@ NERF_API NerfStatus nerf_b200_train_step_profiled(void* context, NerfB200StepPro
     for (auto& e : ev)
         if (cudaEventCreate(&e) != cudaSuccess) st = NERF_STATUS_CUDA_ERROR;
     if (st == NERF_STATUS_OK && c->enqueue_step(c->stream, ev) != cudaSuccess) st = NERF_STATUS_CUDA_ERROR;
+    if (st == NERF_STATUS_OK) c->stats_host_current = true;
     if (st == NERF_STATUS_OK && cudaStreamSynchronize(c->stream) != cudaSuccess) st = NERF_STATUS_CUDA_ERROR;
     if (st == NERF_STATUS_OK) {
         for (int k = 0; k < nb::kStepKernels; ++k) cudaEventElapsedTime(&out->milliseconds[k], ev[k], ev[k + 1]);

@@ -201,6 +201,7 @@ struct OptimArgs {
     DpPeers dp;
     const float* mlp_in;         // MLP gradients + loss read by statistics and Adam (mlp_grad, or dp.mlp_sum)
     uint32_t fuse_wgrad;         // statistics kernel also reduces the weight-gradient partials (single GPU)
+    StatsBlock* stats_host;      // mapped pinned host mirror of the step statistics, or null
 };
 cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);

@@ -178,6 +178,15 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     st->stats.has_nonfinite = has_nonfinite;
     st->stats.completed_steps = step;
     st->stats.last_train_camera = train_camera(frame, tc.n_images);
+    if (a.stats_host) {  // the host reads the statistics without a copy
+        volatile StatsBlock* h = a.stats_host;
+        h->loss = loss;
+        h->grad_norm = grad_norm;
+        h->has_nonfinite = has_nonfinite;
+        h->completed_steps = step;
+        h->last_train_camera = train_camera(frame, tc.n_images);
+        __threadfence_system();
+    }
     AdamScalars sc;
     adam_scalars(tc, grad_norm, has_nonfinite, step, sc);
     st->adam = sc;
