@@ -451,11 +451,11 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     NB_TRY(cudaMemcpyAsync(cams, d.cameras_4x4_packed, n_images * 64ull, cudaMemcpyHostToDevice, stream));
     NB_TRY(cudaMemsetAsync(inference_rgba, 0, static_cast<uint64_t>(width) * height * 4u, stream));
 
-    // parameters: hash table U(-s, s), MLPs with the reference's Xavier draw
-    std::vector<float> host(n_params);
-    SplitMix hash_rng(0x2468ull, 0x1357ull);
-    for (uint64_t i = 0; i < n_grid; ++i) host[i] = hash_rng.unit() * opt.hash_init_scale;
-    float* mlp = host.data() + n_grid;
+    // parameters: hash table U(-s, s) (its splitmix stream drawn on the device,
+    // one thread per value), MLPs with the reference's Xavier draw
+    std::vector<float> host(kMlpParams);
+    NB_TRY(launch_splitmix_fill(master, n_grid, SplitMix(0x2468ull, 0x1357ull).state, opt.hash_init_scale, stream));
+    float* mlp = host.data();
     SplitMix dens(0x1234ull, 0x5678ull);
     xavier(dens, 32, 64, mlp + kMlpD0);
     xavier(dens, 64, 16, mlp + kMlpD1);
@@ -463,7 +463,7 @@ NerfStatus Context::init(const NerfCreateDesc& d, const NerfB200Options& o) {
     xavier(col, 32, 64, mlp + kMlpC0);
     xavier(col, 64, 64, mlp + kMlpC1);
     xavier(col, 64, 16, mlp + kMlpC2);
-    NB_TRY(cudaMemcpyAsync(master, host.data(), n_params * 4, cudaMemcpyHostToDevice, stream));
+    NB_TRY(cudaMemcpyAsync(master + n_grid, host.data(), kMlpParams * 4, cudaMemcpyHostToDevice, stream));
     NB_TRY(launch_f32_to_f16(master, p16, n_params, stream));
     NB_TRY(cudaMemsetAsync(m, 0, n_params * 4, stream));
     NB_TRY(cudaMemsetAsync(v, 0, n_params * 4, stream));

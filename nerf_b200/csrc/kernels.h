@@ -208,6 +208,9 @@ cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s);
 uint32_t grad_stats_blocks(uint64_t n_params);
 cudaError_t launch_f32_to_f16(const float* src, void* dst, uint64_t n, cudaStream_t s);
+// dst[i] = scale * draw i of the splitmix64 stream whose state is state0 before
+// the first draw (a uniform in [-1, 1) from the top 24 bits of each draw).
+cudaError_t launch_splitmix_fill(float* dst, uint64_t n, uint64_t state0, float scale, cudaStream_t s);
 // Sum of every rank's grid gradients over the owned range into dp.gsum and of
 // every rank's MLP gradients into dp.mlp_sum; the owned range's sum of squares
 // and non-finite flag go to every rank's DpSync::partials.

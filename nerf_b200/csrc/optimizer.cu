@@ -444,6 +444,23 @@ __global__ void k_f32_to_f16(const float* __restrict__ src, __half* __restrict__
         dst[i] = __float2half_rn(src[i]);
 }
 
+// dst[i] = scale * (draw i of a splitmix64 stream from state0), the draw a
+// uniform in [-1, 1) from its top 24 bits.  splitmix64's state advances by a
+// constant per draw, so draw i is a function of i alone and the fill runs one
+// thread per value, bit-identical to drawing the stream in order.
+__global__ void k_splitmix_fill(float* __restrict__ dst, uint64_t n, uint64_t state0, float scale) {
+    for (uint64_t i = static_cast<uint64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+        uint64_t z = state0 + (i + 1u) * 0x9e3779b97f4a7c15ull;
+        z = (z ^ (z >> 30u)) * 0xbf58476d1ce4e5b9ull;
+        z = (z ^ (z >> 27u)) * 0x94d049bb133111ebull;
+        z ^= z >> 31u;
+        const float u24 = static_cast<float>(static_cast<uint32_t>(z >> 32u) >> 8u);
+        const float unit = __fsub_rn(__fmul_rn(__fmul_rn(u24, 1.0f / 16777216.0f), 2.0f), 1.0f);
+        dst[i] = __fmul_rn(unit, scale);
+    }
+}
+
 uint32_t g_sms = 0;
 uint32_t sm_count() {
     if (g_sms == 0u) {
@@ -496,6 +513,12 @@ cudaError_t launch_f32_to_f16(const float* src, void* dst, uint64_t n, cudaStrea
     uint64_t blocks = (n + 255u) / 256u;
     if (blocks > 4096u) blocks = 4096u;
     k_f32_to_f16<<<static_cast<uint32_t>(blocks), 256, 0, s>>>(src, static_cast<__half*>(dst), n);
+    return cudaGetLastError();
+}
+cudaError_t launch_splitmix_fill(float* dst, uint64_t n, uint64_t state0, float scale, cudaStream_t s) {
+    if (n == 0u) return cudaSuccess;
+    const uint64_t want = (n + 255u) / 256u, cap = 8ull * sm_count();
+    k_splitmix_fill<<<static_cast<uint32_t>(want < cap ? want : cap), 256, 0, s>>>(dst, n, state0, scale);
     return cudaGetLastError();
 }
 
