@@ -120,7 +120,6 @@ struct SamplerArgs {
     uint32_t* sample_ray;     // [sample_cap]
     uint32_t* ray_index;      // [max_rays] compacted -> marched ray index
 };
-constexpr uint32_t kSamplerBlock = 256;
 // Step recurrence of every ray of the step whose frame is in the state.  A
 // step's march only depends on the frame and the ray count, so the training
 // step ends with the next step's march.

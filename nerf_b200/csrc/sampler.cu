@@ -109,49 +109,53 @@ __global__ void __launch_bounds__(kMarchBlock) k_march(const SamplerArgs a) {
     a.geom[r] = g;
 }
 
-__device__ __forceinline__ uint32_t warps_in_grid() { return gridDim.x * (blockDim.x / 32u); }
-__device__ __forceinline__ uint32_t warp_in_grid() { return blockIdx.x * (blockDim.x / 32u) + (threadIdx.x >> 5); }
 
-// Bitfield tests: a grid-stride loop over rays, one warp each.  Lane c takes
-// chunk c (32 consecutive steps): from the chunk's stored start it runs the
-// march's own rounded recurrence, so every t is the march's bit for bit, and
-// tests each step's midpoint against the bitfield.  A warp scan of the
-// chunks' kept counts places each lane's kept steps in the ray's kept list
-// ([ray][max_steps], step order), which a second walk of the chunk fills
-// with their t.  The ray's sample count is the warp's total.
-__global__ void __launch_bounds__(kSamplerBlock) k_sample_bits(const SamplerArgs a) {
+// Bitfield tests: a grid-stride loop over rays, one 128-thread block each.
+// Thread k takes steps 8k..8k+7 of each 1024-step group: from the stored start
+// of their 32-step chunk it runs the march's own rounded recurrence to its
+// first step and on through its eight (so every t is the march's, bit for
+// bit), computes the eight occupancy cells and issues their bitfield loads
+// together.  A block scan of the threads' kept counts places each thread's
+// kept steps in the ray's kept list ([ray][max_steps], step order), which a
+// second walk of its steps fills with their t.  The ray's sample count is the
+// block's total.  (A warp per ray with a lane per chunk left the SMs idle
+// three quarters of the time: too few warps, each with 32 serial lookups.)
+constexpr uint32_t kBitsThreads = 128, kBitsSteps = 8;
+__global__ void __launch_bounds__(kBitsThreads) k_sample_bits(const SamplerArgs a) {
+    __shared__ uint32_t warp_total[kBitsThreads / 32u];
     const TrainConsts& tc = a.tc;
     const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
     uint32_t* counts = counts_of(a, a.state->frame_index);
-    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const AabbConsts box = aabb_of(tc);
-    for (uint32_t r = warp_in_grid(); r < n_rays; r += warps_in_grid()) {
+    for (uint32_t r = blockIdx.x; r < n_rays; r += gridDim.x) {
         const RayGeom g = a.geom[r];
         const float* ct = a.chunk_t + static_cast<unsigned long long>(r) * tc.mask_words;
         float* kt = a.kept_t + static_cast<unsigned long long>(r) * tc.max_steps;
         uint32_t kept = 0u;
-        for (uint32_t c0 = 0; 32u * c0 < g.n_steps; c0 += 32u) {
-            const uint32_t first = 32u * (c0 + lane);
-            const uint32_t m = first < g.n_steps ? min(32u, g.n_steps - first) : 0u;
-            const float t0 = m ? ct[c0 + lane] : 0.0f;
-            // Eight cell indices at a time, then their eight bitfield loads
-            // in flight together.
+        for (uint32_t s0 = 0; s0 < g.n_steps; s0 += kBitsThreads * kBitsSteps) {
+            const uint32_t first = s0 + threadIdx.x * kBitsSteps;
+            const uint32_t m = first < g.n_steps ? min(kBitsSteps, g.n_steps - first) : 0u;
+            float t0 = 0.0f;
             uint32_t bits = 0u;
-            float t = t0;
-            for (uint32_t j0 = 0; j0 < m; j0 += 8u) {
-                uint32_t cell[8];
+            if (m) {
+                float t = ct[first >> 5];
+                for (uint32_t j = first & 31u; j > 0u; --j) t = __fadd_rn(t, march_dt(t, g.tf, g.dt_min, tc.cone));
+                t0 = t;
+                uint32_t cell[kBitsSteps];
 #pragma unroll
-                for (uint32_t j = 0; j < 8u; ++j) {
+                for (uint32_t j = 0; j < kBitsSteps; ++j) {
                     const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
                     const float mid = march_mid(t, dt);
                     const float p[3] = {__fmaf_rn(mid, g.d[0], g.o[0]), __fmaf_rn(mid, g.d[1], g.o[1]),
                                         __fmaf_rn(mid, g.d[2], g.o[2])};
-                    cell[j] = j0 + j < m ? occupancy_cell(tc.grid_res, box, p) : kNoCell;
+                    cell[j] = j < m ? occupancy_cell(tc.grid_res, box, p) : kNoCell;
                     t = __fadd_rn(t, dt);
                 }
 #pragma unroll
-                for (uint32_t j = 0; j < 8u; ++j) bits |= cell_bit(a.bitfield, cell[j]) ? 1u << (j0 + j) : 0u;
+                for (uint32_t j = 0; j < kBitsSteps; ++j) bits |= cell_bit(a.bitfield, cell[j]) ? 1u << j : 0u;
             }
+            // Exclusive scan of the kept counts in thread order.
             const uint32_t cnt = static_cast<uint32_t>(__popc(bits));
             uint32_t incl = cnt;
 #pragma unroll
@@ -159,17 +163,27 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_bits(const SamplerArgs
                 const uint32_t x = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= static_cast<uint32_t>(o)) incl += x;
             }
-            uint32_t out = kept + incl - cnt;
-            t = t0;
-            for (uint32_t left = bits; left; ) {
+            if (lane == 31u) warp_total[warp] = incl;
+            __syncthreads();
+            uint32_t before = 0u, total = 0u;
+#pragma unroll
+            for (uint32_t w = 0; w < kBitsThreads / 32u; ++w) {
+                const uint32_t v = warp_total[w];
+                before += w < warp ? v : 0u;
+                total += v;
+            }
+            __syncthreads();  // warp_total is rewritten by the next group
+            uint32_t out = kept + before + incl - cnt;
+            float t = t0;
+            for (uint32_t left = bits; left;) {
                 const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
                 if (left & 1u) kt[out++] = t;
                 left >>= 1;
                 t = __fadd_rn(t, dt);
             }
-            kept += __shfl_sync(0xffffffffu, incl, 31);
+            kept += total;
         }
-        if (lane == 0u) counts[r] = kept;
+        if (threadIdx.x == 0u) counts[r] = kept;
     }
 }
 
@@ -317,27 +331,31 @@ __device__ __forceinline__ void write_record(const SamplerArgs& a, const RayGeom
     a.rays[slot] = rec;
 }
 
-// One warp per kept ray (grid-stride): lane k writes samples k, k+32, ...
-// of the ray at their final offsets, each from its t in the ray's kept list
-// (midpoint position and dt as the march defines them).
-__global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArgs a) {
+// One 128-thread block per kept ray (grid-stride): thread k writes samples
+// k, k+128, ... of the ray at their final offsets, each from its t in the
+// ray's kept list (midpoint position and dt as the march defines them);
+// threads 0-3 fetch the ray record's four ground-truth texels first.
+constexpr uint32_t kWriteThreads = 128;
+__global__ void __launch_bounds__(kWriteThreads) k_sample_write(const SamplerArgs a) {
     const TrainConsts& tc = a.tc;
     const uint32_t frame = a.state->frame_index;
     const uint32_t camera = train_camera(frame, tc.n_images);
     const uint32_t n_rays = min(a.state->n_rays, tc.max_rays);
-    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t tid = threadIdx.x;
     const uint32_t* counts = counts_of(a, frame);
-    for (uint32_t r = warp_in_grid(); r < n_rays; r += warps_in_grid()) {
+    for (uint32_t r = blockIdx.x; r < n_rays; r += gridDim.x) {
         const uint32_t count = counts[r], slot = a.ray_slot[r], excl = a.ray_offset[r];
         if (count == 0u || slot == 0xFFFFFFFFu) continue;
         const RayGeom g = a.geom[r];
-        // Lanes 0-3 fetch the record's four texels before the samples.
-        const Footprint f = footprint(tc, g, camera);
-        const unsigned long long ti = (lane & 2u) ? ((lane & 1u) ? f.texel[3] : f.texel[2]) : ((lane & 1u) ? f.texel[1] : f.texel[0]);
-        const uint32_t texel = lane < 4u ? __ldg(reinterpret_cast<const uint32_t*>(a.images) + ti) : 0u;
+        Footprint f{};
+        uint32_t texel = 0u;
+        if (tid < 4u) {
+            f = footprint(tc, g, camera);
+            const unsigned long long ti = (tid & 2u) ? ((tid & 1u) ? f.texel[3] : f.texel[2]) : ((tid & 1u) ? f.texel[1] : f.texel[0]);
+            texel = __ldg(reinterpret_cast<const uint32_t*>(a.images) + ti);
+        }
         const float* kt = a.kept_t + static_cast<unsigned long long>(r) * tc.max_steps;
-#pragma unroll 4
-        for (uint32_t si = lane; si < count; si += 32u) {
+        for (uint32_t si = tid; si < count; si += kWriteThreads) {
             const float t = kt[si];
             const float dt = march_dt(t, g.tf, g.dt_min, tc.cone);
             const float mid = march_mid(t, dt);
@@ -345,9 +363,11 @@ __global__ void __launch_bounds__(kSamplerBlock) k_sample_write(const SamplerArg
                                               __fmaf_rn(mid, g.d[2], g.o[2]), dt);
             a.sample_ray[excl + si] = slot;
         }
-        const uint32_t q00 = __shfl_sync(0xffffffffu, texel, 0), q10 = __shfl_sync(0xffffffffu, texel, 1);
-        const uint32_t q01 = __shfl_sync(0xffffffffu, texel, 2), q11 = __shfl_sync(0xffffffffu, texel, 3);
-        if (lane == 0u) write_record(a, g, r, slot, excl, count, frame, f, q00, q10, q01, q11);
+        if (tid < 32u) {  // warp 0
+            const uint32_t q00 = __shfl_sync(0xffffffffu, texel, 0), q10 = __shfl_sync(0xffffffffu, texel, 1);
+            const uint32_t q01 = __shfl_sync(0xffffffffu, texel, 2), q11 = __shfl_sync(0xffffffffu, texel, 3);
+            if (tid == 0u) write_record(a, g, r, slot, excl, count, frame, f, q00, q10, q01, q11);
+        }
     }
 }
 
@@ -359,21 +379,22 @@ cudaError_t launch_march(const SamplerArgs& a, cudaStream_t s) {
 }
 
 namespace {
-cudaError_t warp_blocks(uint32_t* blocks) {  // grid-stride kernels: 8 blocks per SM
+cudaError_t sm_blocks(uint32_t per_sm, uint32_t* blocks) {  // grid-stride kernels: blocks per SM x SMs
     int dev = 0, sms = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
-    *blocks = static_cast<uint32_t>(sms) * 8u;
+    *blocks = static_cast<uint32_t>(sms) * per_sm;
     return cudaSuccess;
 }
 }  // namespace
 
+// 16 resident blocks of 128 threads per SM: every SM takes rays from the start.
 cudaError_t launch_sample_bits(const SamplerArgs& a, cudaStream_t s) {
     uint32_t blocks = 0;
-    cudaError_t e = warp_blocks(&blocks);
+    cudaError_t e = sm_blocks(16u, &blocks);
     if (e != cudaSuccess) return e;
-    k_sample_bits<<<blocks, kSamplerBlock, 0, s>>>(a);
+    k_sample_bits<<<blocks, kBitsThreads, 0, s>>>(a);
     return cudaGetLastError();
 }
 
@@ -384,9 +405,9 @@ cudaError_t launch_sample_scan(const SamplerArgs& a, cudaStream_t s) {
 
 cudaError_t launch_sample_write(const SamplerArgs& a, cudaStream_t s) {
     uint32_t blocks = 0;
-    cudaError_t e = warp_blocks(&blocks);
+    cudaError_t e = sm_blocks(16u, &blocks);
     if (e != cudaSuccess) return e;
-    k_sample_write<<<blocks, kSamplerBlock, 0, s>>>(a);
+    k_sample_write<<<blocks, kWriteThreads, 0, s>>>(a);
     return cudaGetLastError();
 }
 
