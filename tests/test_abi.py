@@ -131,3 +131,30 @@ def test_scene_generator_is_deterministic_and_sane():
     c = nerf_b200.make_scene(kind=1, seed=3, n_primitives=12, density=100.0, extent=1.0, size_min=0.1, size_max=0.6,
                              n_views=2, width=24, height=24, radius=4.0, camera_mode=1, n_threads=2)
     assert (c.cameras[:, 2, 3] > 0).all()  # upper hemisphere
+
+
+def test_extension_struct_mirrors_match_c_layout(tmp_path):
+    """Every NerfB200* ctypes mirror in nerf_b200.abi has the size and field offsets of its C struct in
+    include/nerf_b200.h (compiled probe), and the step profile has one slot per named segment."""
+    import inspect
+    structs = {n: c for n, c in inspect.getmembers(abi, inspect.isclass)
+               if n.startswith("NerfB200") and issubclass(c, C.Structure)}
+    assert "NerfB200StepProfile" in structs and "NerfB200Options" in structs
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "nerf_b200.h"', "int main(void) {"]
+    for n, c in structs.items():
+        lines.append(f'printf("{n}.__size__ %zu\\n", sizeof({n}));')
+        for fname, _ in c._fields_:
+            lines.append(f'printf("{n}.{fname} %zu\\n", offsetof({n}, {fname}));')
+    lines.append('printf("NERF_B200_STEP_KERNELS %d\\n", NERF_B200_STEP_KERNELS);')
+    lines.append("return 0; }")
+    src = tmp_path / "probe.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-std=c11", "-I", str(ROOT / "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.rsplit(" ", 1) for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                          check=True).stdout.splitlines())
+    for n, c in structs.items():
+        assert C.sizeof(c) == int(got[f"{n}.__size__"]), n
+        for fname, _ in c._fields_:
+            assert getattr(c, fname).offset == int(got[f"{n}.{fname}"]), (n, fname)
+    assert int(got["NERF_B200_STEP_KERNELS"]) == len(abi.STEP_KERNELS)
