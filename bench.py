@@ -72,6 +72,17 @@ def workload_name():
     return WORKLOAD4 if CONFIG == 4 else WORKLOAD
 
 
+def metric_name():
+    return f"train samples/s (config {CONFIG}, steady state)"
+
+
+def config_dict(args):
+    """The workload both arms run (the same dict in the reference arm's line)."""
+    return {"workload": workload_name(), "pretrain_steps": args.pretrain,
+            "l2": "inputs larger than L2: each step streams the 171 MB fp32 master/m/v through Adam and reads a 256 MB "
+                  "image set; the 24 MB hash table is meant to stay L2-resident"}
+
+
 def options(nb, **kw):
     if CONFIG == 4:
         return nb.default_options(log2_hashmap_size=22, max_resolution=8192, background=1, stop_transmittance=1e-4,
@@ -162,15 +173,26 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def make_dataset(nb, views=None):
+def make_dataset(nb, views=None, renderer=None):
+    """The training views of the workload.  renderer: the scene function (default nb.make_scene, the product
+    library's copy of the scene renderer; the reference arm passes oracle_scene, the oracle library's copy of the
+    same source, so that it never loads libnerf_b200.so)."""
     cfg = dict(scene_cfg())
     if views is not None:
         cfg["n_views"] = views
     if CONFIG == 4:  # the ring is shared out over the views actually rendered
         cfg["orbit_views"] = cfg["n_views"]
     t0 = time.time()
-    ds = nb.make_scene(**cfg)
+    ds = (renderer or nb.make_scene)(**cfg)
     return ds, time.time() - t0
+
+
+def oracle_scene(**cfg):
+    """nb.make_scene through the oracle library (oracle_scene_render: the same scene.cpp, built into liboracle.so)."""
+    import nerf_b200 as nb  # the Dataset container only; this loads no native library
+    from oracle import oracle
+    imgs, cams, intr = oracle.make_scene(**cfg)
+    return nb.Dataset(imgs, cams, intr)
 
 
 # ------------------------------------------------------------------ our arm
@@ -258,17 +280,8 @@ def run_ours(args):
         prof_samples += ctx.counters().total_samples - cb.total_samples
     prof /= max(1, n_prof)
     mean_samples = prof_samples / max(1, n_prof)
-    kernels = kernel_table(ctx, prof, mean_samples)
-    l2 = l2_peaks(lib, stream)
-    for k in kernels:  # L2-bound field kernels against the measured L2 peaks
-        if k["ms"] <= 0.0:
-            continue
-        if k["kernel"] == "field_forward":
-            k["l2_gather_gbs"] = mean_samples * 128 * 4 / (k["ms"] / 1e3) / 1e9
-            k["l2_frac"] = k["l2_gather_gbs"] / l2["read_gbs"]
-        if k["kernel"] == "field_backward":
-            k["corner_updates_g_per_s"] = mean_samples * 128 / (k["ms"] / 1e3) / 1e9
-            k["l2_red_frac"] = k["corner_updates_g_per_s"] / l2["red_f16x2_gops"]
+    l2 = l2_peaks(stream)
+    kernels = kernel_table(ctx, prof, mean_samples, l2, world)
 
     psnr = psnr_heldout(nb, ctx, args) if rank == 0 else None
     render = None
@@ -282,28 +295,25 @@ def run_ours(args):
         e2e = run_e2e(nb, lib, ds_pinned, rank, world, uid, args)
 
     cpu = None
-    if rank == 0 and not args.skip_cpu:
-        cpu = cpu_baseline(nb, ds, args)
+    if rank == 0 and world == 1 and not args.skip_cpu:  # the CPU baseline: rank 0 at N = 1 only
+        cpu = cpu_baseline(ds, args)
     dio = None
     if rank == 0 and not args.skip_dataset_io:
         dio = dataset_io(lib, ds)
 
     if rank == 0:
-        hbm, src = peaks()
-        dom = max(kernels, key=lambda k: k["ms"])
         line = {
-            "metric": f"train samples/s (config {CONFIG}, steady state)",
+            "metric": metric_name(),
             "value": value, "unit": "samples/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f16 (fp32 accumulate, fp32 Adam masters)", "data": "synthetic",
-            "config": {"workload": workload_name(), "parallelism": f"dp{world}", "pretrain_steps": args.pretrain,
-                       "samples_per_step": samples_all / args.steps, "rays_per_step": rays_all / args.steps,
-                       "l2": "inputs larger than L2: each step streams the 171 MB fp32 master/m/v through Adam and "
-                             "reads a 256 MB image set; the 24 MB hash table is meant to stay L2-resident",
-                       "final_loss": stats.loss, "dataset_gen_s": gen_s},
+            "config": config_dict(args),
+            "parallelism": f"dp{world}",
+            "run": {"samples_per_step": samples_all / args.steps, "rays_per_step": rays_all / args.steps,
+                    "final_loss": stats.loss, "dataset_gen_s": gen_s},
             "e2e": e2e,
             "gpu_launches": kernels_per_step * args.steps,
-            "roofline": roofline(dom, hbm, src),
+            "roofline": roofline(kernels),
             "l2": l2,
             "kernels": kernels,
             "render": render,
@@ -318,45 +328,116 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def kernel_table(ctx, prof_ms, samples):
-    """Algorithmic bytes per launch for each step kernel (the per-unit figures are in the comments below)."""
+# Per training sample, from one ncu capture of this build's step kernels on config 2: L2 sectors the forward's
+# gathers request from L2 (hash-table lookups after coalescing and pairing), and L2 reduction operations the
+# scatter issues (after run merging and .v4 pairing).
+NCU_PER_SAMPLE = {"field_forward_l2_read_sectors": None, "grid_scatter_l2_red_ops": 48.06}
+# DRAM bytes (read + write) per launch from the same capture (cold-cache replay, so the hash table and its gradient
+# count as DRAM traffic although a live step keeps them in L2).
+NCU_TRAFFIC = {"mlp_backward": 36.59e6, "grid_scatter": 73.13e6, "field_forward": 31.67e6, "adam": 311.31e6}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops_sustained": float(d["bf16_tflops_sustained"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def kernel_table(ctx, prof_ms, samples, l2, world):
+    """Each step kernel against the roofline that bounds it.  Algorithmic work per launch (per-unit figures in the
+    comments) / the kernel's mean CUDA-event time in the kernel-by-kernel step, over the measured peak of its bound:
+    HBM copy bandwidth (MEASURED_PEAKS.json), the sustained bf16 tensor rate (same file; these kernels run inside a
+    long step), or the live L2 probes (gathers and f16x2 reductions at hashed addresses, 16-byte reads)."""
     from nerf_b200 import abi
-    n_params = ctx.n_params
-    n_grid = ctx.n_grid
+    pk = measured_peaks()
+    n_params, n_grid = ctx.n_params, ctx.n_grid
     cells = GRID_RES ** 3 * (CASCADES4 if CONFIG == 4 else 1)
+    # (bound, unit, algorithmic amount per launch, note)
     per = {
-        # stored features 64 + dout 16 + pos/dt 16 + ray id 4, and 128 f16x2 read-modify-writes of 4+4 bytes
-        "field_backward": samples * (64 + 16 + 16 + 4 + 128 * 8),
-        # pos/dt 16 + ray id 4 + 128 gathers of 4 bytes + features 64 + raw outputs 16
-        "field_forward": samples * (16 + 4 + 128 * 4 + 64 + 16),
-        # raw 16 + pos/dt 16 read twice, dout 16 written (T parked in dout.x: +4+4)
-        "composite": samples * (2 * 32 + 16 + 8),
-        # fp32 master, m, v read+write (24), fp16 grad read + cleared (4 grid) , fp16 param write (2)
-        "adam": n_grid * 30 + (n_params - n_grid) * 30,
-        "grad_stats": n_grid * 2 + (n_params - n_grid) * 4,
-        "wgrad_reduce": (ctx_partials(ctx) + 1) * 10240 * 4,
-        "occupancy_update": cells * 8 + cells // 8,
+        # one thread per 32-cell word: density read + write 8 B per cell, bitfield word 1/8 B per cell
+        "occupancy_update": ("hbm", cells * 8 + cells // 8),
         # t of every kept step written to the ray's kept list
-        "sample_bits": samples * 4,
+        "sample_bits": ("latency", samples * 4),
         # kept t read, pos/dt 16 + ray id 4 written
-        "sample_write": samples * (4 + 16 + 4),
-        "occupancy_query": 0,
-        "allreduce": n_grid * 2 + 10248 * 4,
+        "sample_write": ("hbm", samples * (4 + 16 + 4)),
+        # 128 corner lookups of 4 B per sample (16 levels x 8 corners), against the hashed 4-byte gather probe;
+        # bytes: pos/dt 16 + ray id 4 + 512 corner bytes + 112 training row + 16 raw out
+        "field_forward": ("l2_gather", samples * 128),
+        # raw 16 + pos/dt 16 read twice, dout 16 written, transmittance 8
+        "composite": ("hbm", samples * (2 * 32 + 16 + 8)),
+        # forward recompute 20,480 + input-gradient 20,480 + weight-gradient 20,480 FLOP per sample
+        "mlp_backward": ("tensor", samples * 61440),
+        # L2 reduction operations issued per sample (ncu), against the .v4 f16x2 reduction probe
+        "grid_scatter": ("l2_red", samples * NCU_PER_SAMPLE["grid_scatter_l2_red_ops"]),
+        # partials: one row of 10240 fp32 per backward CTA read, 10240 sums written
+        "wgrad_reduce": ("hbm", (ctx_partials(ctx) + 1) * 10240 * 4),
+        # fp16 hash gradients 2 B and fp32 MLP gradients 4 B read
+        "grad_stats": ("hbm", n_grid * 2 + (n_params - n_grid) * 4),
+        # fp32 master, m, v read + written (24), fp16 gradient read + cleared (4), fp16 parameter written (2)
+        "adam": ("hbm", n_params * 30),
+        # peer mode: this rank's 1/N of every rank's fp16 hash gradients read over NVLink
+        "allreduce": ("nvlink", n_grid * 2 * (world - 1) / max(world, 1)),
+        "occupancy_query": ("latency", 0),
+        "sample_scan": ("latency", 0),
+        "march": ("latency", 0),
     }
     out = []
     for name, ms in zip(abi.STEP_KERNELS, prof_ms):
-        b = per.get(name, 0)
-        out.append({"kernel": name, "ms": float(ms), "bytes": int(b), "gbs": (b / (ms / 1e3) / 1e9) if ms > 0 else 0.0})
+        bound, amount = per.get(name, ("latency", 0))
+        rec = {"kernel": name, "ms": float(ms), "bound": bound}
+        t = ms / 1e3
+        if ms > 0 and amount:
+            if bound == "hbm":
+                rec.update(achieved=amount / t / 1e9, peak=pk["hbm_gbs"], unit="GB/s")
+            elif bound == "tensor":
+                rec.update(achieved=amount / t / 1e12, peak=pk["bf16_tflops_sustained"], unit="TFLOP/s")
+            elif bound == "l2_gather":
+                rec.update(achieved=amount / t / 1e9, peak=l2["gather_4b_gops"], unit="G lookups/s",
+                           l2_read_gbs=samples * 660 / t / 1e9, l2_read_frac=samples * 660 / t / 1e9 / l2["read_gbs"])
+                sec = NCU_PER_SAMPLE["field_forward_l2_read_sectors"]
+                if sec:
+                    rec["l2_sectors_g_per_s"] = samples * sec / t / 1e9
+            elif bound == "l2_red":
+                rec.update(achieved=amount / t / 1e9, peak=l2["red_v4_f16x2_gops"], unit="G red ops/s",
+                           corner_updates_g_per_s=samples * 128 / t / 1e9)
+            elif bound == "nvlink":
+                rec.update(achieved=amount / t / 1e9, peak=770.0, unit="GB/s")
+            else:
+                rec.update(bytes=int(amount), gbs=amount / t / 1e9)
+            if "peak" in rec:
+                rec["frac"] = rec["achieved"] / rec["peak"]
+        out.append(rec)
     return out
 
 
-def l2_peaks(lib, stream):
-    """L2 peaks of this GPU from the library's probes: 16-byte read bandwidth of
-    an L2-resident 64 MB buffer, and f16x2 / v2.f16x2 reduction rates at hashed
-    addresses of a 32 MB buffer (the shape of the hash-table scatter)."""
+def probe_lib():
+    """libnerf_b200_l2probe.so: the benchmark's L2 microbenchmarks (a library of their own, not part of the
+    product library)."""
+    import ctypes as C
+    path = ROOT / "nerf_b200" / "libnerf_b200_l2probe.so"
+    if not path.exists():
+        raise RuntimeError(f"{path} is not built (make -C nerf_b200/csrc)")
+    lib = C.CDLL(str(path))
+    P, U32 = C.c_void_p, C.c_uint32
+    lib.nerf_b200_probe_l2_read.argtypes = [P, C.c_uint64, U32, P, P]
+    lib.nerf_b200_probe_l2_red.argtypes = [P, U32, U32, U32, C.POINTER(C.c_uint64), P]
+    lib.nerf_b200_probe_l2_gather.argtypes = [P, U32, U32, U32, P, C.POINTER(C.c_uint64), P]
+    for f in (lib.nerf_b200_probe_l2_read, lib.nerf_b200_probe_l2_red, lib.nerf_b200_probe_l2_gather):
+        f.restype = C.c_int
+    return lib
+
+
+def l2_peaks(stream):
+    """L2 peaks of this GPU from the benchmark's probes: 16-byte read bandwidth of an L2-resident 64 MB buffer,
+    4- and 8-byte gathers at hashed addresses of a 32 MB buffer (the shape of the hash-table lookups), and f16x2 /
+    v2 / v4 reduction rates at hashed addresses of the same buffer (the shape of the hash-table scatter)."""
     import ctypes as C
 
     import torch
+    lib = probe_lib()
     h = C.c_void_p(stream.cuda_stream)
     sink = torch.zeros(1024, dtype=torch.int32, device="cuda")
     res = {}
@@ -383,9 +464,12 @@ def l2_peaks(lib, stream):
     for vec, key in ((0, "red_f16x2_gops"), (1, "red_v2_f16x2_gops"), (2, "red_v4_f16x2_gops")):
         t = timed(lambda: lib.nerf_b200_probe_l2_red(rb.data_ptr(), words, 64, vec, C.byref(ops), h))
         res[key] = ops.value / t / 1e9
-    res["note"] = ("probes: 64 MB L2-resident buffer, 16 sweeps of 16-byte loads; f16x2 reductions at hashed word "
-                   "addresses of a 32 MB buffer (v2 / v4: 8- / 16-byte forms), 64 per thread over 8 blocks x 256 "
-                   "threads per SM")
+    for vec, key in ((0, "gather_4b_gops"), (1, "gather_8b_gops")):
+        t = timed(lambda: lib.nerf_b200_probe_l2_gather(rb.data_ptr(), words, 64, vec, sink.data_ptr(), C.byref(ops), h))
+        res[key] = ops.value / t / 1e9
+    res["note"] = ("probes: 64 MB L2-resident buffer, 16 sweeps of 16-byte loads; 4- / 8-byte loads and f16x2 "
+                   "reductions (v2 / v4: 8- / 16-byte forms) at hashed word addresses of a 32 MB buffer, 64 per thread "
+                   "over 8 blocks x 256 threads per SM")
     return res
 
 
@@ -394,20 +478,21 @@ def ctx_partials(ctx):
     return int(abi.load().nerf_b200_field_backward_partial_floats()) // 10240
 
 
-# DRAM bytes (read + write) per launch from one ncu capture of this build
-# (profiles/field_kernels_adam_train_step_config2.md; cold-cache replay, so the
-# hash table and its gradient count as DRAM traffic).  field_backward is the
-# MLP kernel plus the hash scatter kernel.
-NCU_TRAFFIC = {"field_backward": 36.59e6 + 73.13e6, "field_forward": 31.67e6, "adam": 311.31e6}
-
-
-def roofline(dom, hbm, src):
-    achieved = dom["gbs"]
-    return {"kernel": dom["kernel"], "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-            "frac": achieved / hbm, "peak_source": src, "traffic": NCU_TRAFFIC.get(dom["kernel"]),
-            "note": "achieved = algorithmic bytes per launch / mean CUDA-event launch time (kernel-by-kernel step, "
-                    "same kernels as the graph); traffic = ncu DRAM bytes per launch; the field kernels are "
-                    "L2-bound, see the l2 object and the kernels' l2 fractions"}
+def roofline(kernels):
+    """The dominant kernel (longest mean time in the kernel-by-kernel step) against its own bound."""
+    pk = measured_peaks()
+    dom = max((k for k in kernels if "frac" in k), key=lambda k: k["ms"])
+    src = {"hbm": f"MEASURED_PEAKS.json hbm_gbs ({pk['source']})",
+           "tensor": f"MEASURED_PEAKS.json bf16_tflops_sustained ({pk['source']})",
+           "l2_gather": "live probe: 4-byte loads at hashed addresses of an L2-resident 32 MB buffer",
+           "l2_red": "live probe: 16-byte f16x2 reductions at hashed addresses of an L2-resident 32 MB buffer",
+           "nvlink": "measured peer copy, 770 GB/s per direction"}[dom["bound"]]
+    return {"kernel": dom["kernel"], "bound": dom["bound"], "achieved": dom["achieved"], "peak": dom["peak"],
+            "unit": dom["unit"], "frac": dom["frac"], "peak_source": src,
+            "traffic": NCU_TRAFFIC.get(dom["kernel"]),
+            "note": "achieved = algorithmic work per launch / mean CUDA-event launch time (kernel-by-kernel step, "
+                    "same kernels as the graph); traffic = ncu DRAM bytes per launch (cold-cache replay); every "
+                    "step kernel's own bound and fraction is in the kernels list"}
 
 
 def psnr_heldout(nb, ctx, args):
@@ -566,40 +651,44 @@ def dataset_io(lib, ds):
         shutil.rmtree(d, ignore_errors=True)
 
 
-def cpu_baseline(nb, ds, args, steps=None, threads=None, seconds=20.0):
-    """The CPU oracle (restatement of the same algorithm) on a bounded sample of the config-2 workload."""
+def cpu_baseline(ds, args, threads=None, seconds=20.0, max_steps=None):
+    """The CPU oracle (the scalar C++ restatement of the same algorithm) on the workload's own step shape: 4096
+    initial rays, 2^18 target samples per step, 2^19 capacity, <= 1024 steps per ray, on all host threads.  The
+    sample is bounded by wall time, not by shrinking the batch: one untimed step (the fresh job's first step, cut at
+    the 2^19 capacity), then whole steps until `seconds` have passed (at least two).  Returns the samples/s of the
+    timed steps."""
     from oracle import oracle
+    from nerf_b200.abi import NerfCreateDesc
+    import nerf_b200 as nb  # ctypes structures and the training-config builder only; no native library is loaded
     threads = threads or os.cpu_count() or 1
-    opts = options(nb)
-    desc = nb.Context.__new__(nb.Context)
     images = np.ascontiguousarray(ds.images)
     cams = np.ascontiguousarray(ds.cameras)
     fx, fy, cx, cy = ds.intrinsics
-    from nerf_b200.abi import NerfCreateDesc
     d = NerfCreateDesc(GRID_RES, 2 * TARGET_SAMPLES, 1 << 16, 256, images.ctypes.data, images.nbytes, cams.ctypes.data,
                        cams.nbytes, ds.n, ds.width, ds.height, fx, fy, cx, cy)
-    # bounded sample: 1/64 of the per-step sample target, same rays-per-step rule
-    small = TARGET_SAMPLES // 64
-    oc = oracle.Context(d, oracle.options(log2_hashmap_size=19, max_resolution=2048, background=1,
-                                          stop_transmittance=1e-4, target_samples_per_step=small,
-                                          max_samples_per_step=2 * small, n_threads=threads), images, cams)
-    cfg = train_config(nb)
-    cfg.rays_per_batch = 64
-    oc.configure(cfg)
+    big = CONFIG == 4
+    oc = oracle.Context(d, oracle.options(log2_hashmap_size=22 if big else 19, max_resolution=8192 if big else 2048,
+                                          background=1, stop_transmittance=1e-4, target_samples_per_step=TARGET_SAMPLES,
+                                          max_samples_per_step=2 * TARGET_SAMPLES, n_threads=threads,
+                                          n_cascades=CASCADES4 if big else 1), images, cams)
+    oc.configure(train_config(nb))
+    oc.step()  # untimed: the first step of a fresh job (all cells occupied, cut at the capacity)
+    first = oc.info().samples
     t0 = time.perf_counter()
-    samples = 0
-    n = 0
+    samples = n = 0
     while True:
         oc.step()
         samples += oc.info().samples
         n += 1
-        if (steps and n >= steps) or (not steps and time.perf_counter() - t0 > seconds):
+        el = time.perf_counter() - t0
+        if n >= 2 and (el > seconds or (max_steps and n >= max_steps)):
             break
     dt = time.perf_counter() - t0
     oc.close()
     return {"value": samples / dt, "unit": "samples/s", "cores": threads, "kind": "port",
-            "sample": f"{n} oracle training steps of config 2 at {small} target samples/step ({samples} samples, "
-                      f"{dt:.1f} s, warm-up phase of a fresh job)"}
+            "sample": f"{n} whole oracle training steps of config {CONFIG} after one untimed step ({first} samples): "
+                      f"{samples} samples in {dt:.1f} s, 4096 initial rays, 2^18 target samples per step, "
+                      f"occupancy warm-up phase of a fresh job"}
 
 
 # ------------------------------------------------------------ microbench
@@ -633,7 +722,7 @@ def run_micro(args):
     hbm, src = peaks()
     tf_peak = float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"]) \
         if (ROOT / "MEASURED_PEAKS.json").exists() else 1590.0
-    l2 = l2_peaks(lib, stream)
+    l2 = l2_peaks(stream)
     gen = torch.Generator(device="cuda").manual_seed(5)
     reps = args.micro_reps
 
@@ -758,21 +847,21 @@ def run_micro(args):
 
 # ------------------------------------------------------------ reference arm
 def run_reference(args):
+    """The reference arm: the CPU oracle (kind "port": the reference backend has no CPU implementation of the path)
+    on this arm's own workload and config, rank 0 only, with all host threads.  It loads no product library: the
+    dataset comes from the oracle library's copy of the scene renderer.  Its line also carries "reference_cuda", the
+    reference's own CUDA backend (oracle/_ref/libref_stock.so) run in a child process."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import nerf_b200 as nb
-    ds, _ = make_dataset(nb, args.views)
-    threads = os.cpu_count() or 1
-    for _ in range(args.warmup):
-        pass
-    res = cpu_baseline(nb, ds, args, steps=max(1, args.steps), threads=threads)
+    ds, _ = make_dataset(None, args.views, renderer=oracle_scene)
+    res = cpu_baseline(ds, args, seconds=args.reference_seconds)
     ref_cuda = None if args.skip_reference_cuda else reference_cuda(args)
-    line = {"metric": "train samples/s (config 2, steady state)", "value": res["value"], "unit": "samples/s",
+    line = {"metric": metric_name(), "value": res["value"], "unit": "samples/s",
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": None, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32 (fp16-rounded operands)", "data": "synthetic", "impl": "reference",
-            "config": {"workload": WORKLOAD, "parallelism": "cpu"},
+            "config": config_dict(args), "parallelism": "cpu",
             "cpu_baseline": res,
             "e2e": {"value": res["value"], "unit": "samples/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "reference_cuda": ref_cuda}
@@ -826,6 +915,8 @@ def main():
     ap.add_argument("--micro-rows", type=int, nargs="*", default=[16, 18, 20, 22])
     ap.add_argument("--micro-samples", type=int, nargs="*", default=[1, 16, 64, 256, 1024])
     ap.add_argument("--reference-cuda-steps", type=int, default=200)
+    ap.add_argument("--reference-seconds", type=float, default=30.0,
+                    help="wall time of the reference arm's timed CPU-oracle steps")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

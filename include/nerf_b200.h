@@ -73,10 +73,11 @@ NERF_API NerfStatus nerf_b200_context_stream(void* context, void** stream);
 /* One training step launched kernel by kernel instead of as the captured
  * graph, with CUDA events between launches.  Segments: occupancy query,
  * occupancy update, sampler bitfield tests, compaction scan, sample writes,
- * field forward, composite, field backward, weight-gradient reduce (folded
- * into the statistics on one GPU), gradient exchange (0 on one GPU),
- * gradient statistics, the next step's ray march, Adam. */
-#define NERF_B200_STEP_KERNELS 13
+ * field forward, composite, MLP backward, hash-table gradient scatter,
+ * weight-gradient reduce (folded into the statistics on one GPU), gradient
+ * exchange (0 on one GPU), gradient statistics, the next step's ray march,
+ * Adam. */
+#define NERF_B200_STEP_KERNELS 14
 typedef struct NerfB200StepProfile {
     float milliseconds[NERF_B200_STEP_KERNELS];
     float total_milliseconds;
@@ -300,11 +301,14 @@ NERF_API NerfStatus nerf_b200_mlp_backward(const void* mlp_params_f16, const voi
  * scratch lives in a static device array of
  * nerf_b200_field_backward_noalloc_max_rows() x 10240 floats (13.1 MB, held
  * by every GPU that loads the library until exit); the call fails with
- * NERF_STATUS_INVALID_USAGE when this GPU needs more rows (more than 160
- * SMs) or n exceeds 2^31-1.  The first call on a device looks up the array's
- * device address; make it before any stream capture.  Calls share the array:
- * calls that overlap on the GPU race.  Other arguments as in
- * nerf_b200_field_backward. */
+ * NERF_STATUS_INVALID_USAGE when this GPU needs more rows, that is when
+ * nerf_b200_field_backward_partial_floats() / 10240 exceeds
+ * nerf_b200_field_backward_noalloc_max_rows(), or when n exceeds 2^31-1.
+ * The first call on a device looks up the array's device address; make it
+ * before any stream capture.  The address is kept for the process: after a
+ * cudaDeviceReset of that device do not call this entry point again.  Calls
+ * share the array: calls that overlap on the GPU race.  Other arguments as
+ * in nerf_b200_field_backward. */
 NERF_API uint32_t nerf_b200_field_backward_noalloc_max_rows(void);
 NERF_API NerfStatus nerf_b200_field_backward_noalloc(const NerfB200GridLayout* layout, const void* params_f16,
                                                      const float* pos_unit, const float* dirs, uint32_t n,
@@ -329,20 +333,6 @@ NERF_API NerfStatus nerf_b200_adam(float* master, void* params_f16, void* grid_g
 NERF_API NerfStatus nerf_b200_occupancy_update(float* density, uint32_t* bitfield, const float* sigma, uint32_t cell_count,
                                                uint32_t update_count, uint32_t frame_index, uint32_t mode, float decay,
                                                float threshold, void* stream);
-
-/* ---------------------------------------------------------- measurement */
-/* L2 microbenchmarks (no counterpart in the reference) giving the L2 peaks
- * the hash-grid kernels are measured against.  Both launch asynchronously on
- * `stream`; the caller times them with events.
- * read: `passes` sweeps of 16-byte loads over `bytes` of `buf` (16-byte
- *       aligned; `sink` >= 1024 words, written only to keep loads live).
- * red:  reps f16x2 reductions per thread (vec 0: 4-byte form, 1: 8-byte
- *       .v2, 2: 16-byte .v4) at hashed word indices of `buf` (16-byte
- *       aligned, `words` a power of two >= 4); *ops receives the number of
- *       reduction instructions issued. */
-NERF_API NerfStatus nerf_b200_probe_l2_read(const void* buf, uint64_t bytes, uint32_t passes, uint32_t* sink, void* stream);
-NERF_API NerfStatus nerf_b200_probe_l2_red(void* buf, uint32_t words, uint32_t reps, uint32_t vec, uint64_t* ops,
-                                           void* stream);
 
 #ifdef __cplusplus
 }

@@ -208,7 +208,7 @@ class NerfB200RenderInfo(C.Structure):
 
 
 STEP_KERNELS = ["occupancy_query", "occupancy_update", "sample_bits", "sample_scan", "sample_write", "field_forward",
-                "composite", "field_backward", "wgrad_reduce", "allreduce", "grad_stats", "march", "adam"]
+                "composite", "mlp_backward", "grid_scatter", "wgrad_reduce", "allreduce", "grad_stats", "march", "adam"]
 
 
 class NerfB200StepProfile(C.Structure):
@@ -298,8 +298,6 @@ B200_EXPORTS = {
     "nerf_b200_load_training_state": (S, [P, C.c_char_p]),
     "nerf_b200_field_backward_noalloc_max_rows": (U32, []),
     "nerf_b200_field_backward_noalloc": (S, [C.POINTER(NerfB200GridLayout), P, P, P, U32, P, P, P, P, P]),
-    "nerf_b200_probe_l2_read": (S, [P, C.c_uint64, U32, P, P]),
-    "nerf_b200_probe_l2_red": (S, [P, U32, U32, U32, C.POINTER(C.c_uint64), P]),
     "nerf_b200_composite": (S, [P, U32, P, P, F32, F32, F32, P, P, P, P, P]),
     "nerf_b200_adam": (S, [P, P, P, P, P, P, U64, U64, P, U32, F32, F32, F32, P]),
     "nerf_b200_occupancy_update": (S, [P, P, P, U32, U32, U32, U32, F32, F32, P]),

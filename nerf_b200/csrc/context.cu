@@ -47,7 +47,7 @@ static_assert(sizeof(NerfB200RayRecord) == sizeof(RayRecord), "ray record mirror
 static_assert(sizeof(StatsBlock) == sizeof(NerfTrainStats), "stats mirror");
 
 constexpr uint32_t kMaxStepsPerRay = 4096;  // the reference allows 256
-constexpr int kStepKernels = 13;            // timed segments of one training step
+constexpr int kStepKernels = 14;            // timed segments of one training step
 
 // ---------------------------------------------------------------- helpers
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1u) / a * a; }
@@ -144,16 +144,6 @@ NerfStatus cuda_status(cudaError_t e) { return e == cudaSuccess ? NERF_STATUS_OK
 // Kernel attributes are set once per device.
 std::mutex g_attr_mu;
 bool g_attr_done[64] = {};
-cudaError_t ensure_attributes() {
-    int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess) return e;
-    std::lock_guard<std::mutex> lk(g_attr_mu);
-    if (dev >= 0 && dev < 64 && g_attr_done[dev]) return cudaSuccess;
-    e = field_init_attributes();
-    if (e == cudaSuccess && dev >= 0 && dev < 64) g_attr_done[dev] = true;
-    return e;
-}
 
 // ------------------------------------------------------ NCCL (loaded lazily)
 struct Nccl {
@@ -183,6 +173,17 @@ Nccl g_nccl;
 std::mutex g_nccl_mu;
 
 }  // namespace
+
+cudaError_t ensure_attributes() {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lk(g_attr_mu);
+    if (dev >= 0 && dev < 64 && g_attr_done[dev]) return cudaSuccess;
+    e = field_init_attributes();
+    if (e == cudaSuccess && dev >= 0 && dev < 64) g_attr_done[dev] = true;
+    return e;
+}
 
 // ------------------------------------------------------------------ context
 struct Context {
@@ -713,15 +714,16 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     }
     if ((e = mark()) != cudaSuccess) return e;
     if ((e = launch_composite(ca, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
-    if (mlp_tc) {  // MLP backward on tcgen05 (writes the feature gradients), then the hash-table scatter
+    // MLP backward (writes the feature gradients), then the hash-table scatter.
+    if (mlp_tc) {  // on tcgen05
         if ((e = launch_mlp_backward_tc(p16 + n_grid, feat, 1, nullptr, reinterpret_cast<const float*>(dout), &state->n_samples, 0u,
-                                        dfeat, partials, n_partials, &state->mlp_error, s)) != cudaSuccess ||
-            (e = launch_grid_scatter(fa, s)) != cudaSuccess)
+                                        dfeat, partials, n_partials, &state->mlp_error, s)) != cudaSuccess)
             return e;
     } else if ((e = launch_field_backward(fa, kFieldTrain, n_partials, s)) != cudaSuccess) {
         return e;
     }
     if ((e = mark()) != cudaSuccess) return e;
+    if ((e = launch_grid_scatter(fa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     // One GPU: the statistics kernel also reduces the weight-gradient partials.
     op.fuse_wgrad = comm ? 0u : 1u;
     op.stats_host = stats_host_dev;
@@ -1681,6 +1683,7 @@ NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, c
                                              void* grid_grad, float* partials, float* mlp_grad, void* stream) {
     if (!layout || layout->n_levels != 16u || !params || !partials || !mlp_grad || !grid_grad) return NERF_STATUS_INVALID_USAGE;
     if (n && (!pos || !dirs || !feat || !dout)) return NERF_STATUS_INVALID_USAGE;
+    if (n > 0x7FFFFFFFu) return NERF_STATUS_INVALID_USAGE;  // rows are indexed with 32-bit tile counters
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
     nb::FieldArgs a{};

@@ -1073,9 +1073,7 @@ cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t blocks,
     if (blocks == 0u) return cudaErrorInvalidValue;
     if ((mode == kFieldTrain || mode == kFieldMlp) && a.dfeat == nullptr) return cudaErrorInvalidValue;
     k_field_backward<<<blocks, kThreads, kBwdSmem, s>>>(a, mode);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess || mode != kFieldTrain) return e;
-    return launch_grid_scatter(a, s);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_grid_scatter(const FieldArgs& a, cudaStream_t s) {

@@ -56,9 +56,9 @@ struct FieldArgs {
     void* dfeat;           // training backward: fp16 n x 32 feature gradients for the scatter kernel
 };
 cudaError_t launch_field_forward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
-// Training mode: MLP backward writing dfeat, then the hash-table scatter
-// kernel.  Direct mode: one fused kernel (MLP backward + scatter).  MLP mode:
-// the MLP backward writing dfeat, no scatter.
+// Training and MLP modes: the MLP backward writing dfeat (the training step
+// then launches the hash-table scatter, launch_grid_scatter).  Direct mode:
+// one fused kernel (MLP backward + scatter).
 cudaError_t launch_field_backward(const FieldArgs& a, int mode, uint32_t grid_blocks, cudaStream_t s);
 // Training forward without the MLPs: hash encode + SH of a.state->n_samples
 // rows into the 112-byte training rows a.feat (launch_mlp_forward_tc_train
@@ -70,6 +70,8 @@ cudaError_t launch_grid_scatter(const FieldArgs& a, cudaStream_t s);
 uint32_t field_forward_blocks();
 uint32_t field_backward_blocks();
 cudaError_t field_init_attributes();
+// field_init_attributes() once per device, under a lock (context.cu).
+cudaError_t ensure_attributes();
 
 // ---- the field MLPs on tcgen05 (mlp_tc.cu) ----
 // Forward of the MLPs on given features (n x 32 fp16) and directions, raw

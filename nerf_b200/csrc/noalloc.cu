@@ -15,7 +15,10 @@
 // until the process exits.  Its device address is looked up once per device
 // with cudaGetSymbolAddress (in host code the symbol name is only a
 // host-side stand-in, not a device address), on the first call made with
-// that device current; make that first call before any stream capture.  All
+// that device current; make that first call before any stream capture.  The
+// cached address belongs to the device's primary context: after a
+// cudaDeviceReset the module is loaded again and the entry point must not be
+// called any more in that process.  All
 // calls share the array: each launch overwrites every row it uses before
 // reading it, so no clearing is needed between calls, but calls whose
 // kernels overlap on the GPU (different streams, or different host threads
@@ -66,7 +69,7 @@ NERF_API NerfStatus nerf_b200_field_backward_noalloc(const NerfB200GridLayout* l
     if (!layout || layout->n_levels != 16u || !params || !mlp_grad || !grid_grad) return NERF_STATUS_INVALID_USAGE;
     if (n && (!pos || !dirs || !feat || !dout)) return NERF_STATUS_INVALID_USAGE;
     if (n > 0x7FFFFFFFu) return NERF_STATUS_INVALID_USAGE;  // rows are indexed with 32-bit tile counters
-    if (nb::field_init_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
+    if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     // Same CTA count as nerf_b200_field_backward, so both give the same sums.
     const uint32_t blocks = nb::field_backward_blocks();
     if (blocks == 0u || blocks > nb::kNoAllocPartialRows) return NERF_STATUS_INVALID_USAGE;  // scratch too small for this GPU

@@ -27,6 +27,14 @@
 
 #include "../../include/nerf_b200.h"
 
+// The exported name.  The CPU oracle's library compiles this same file under
+// another name (oracle_scene_render), so that a process which must not load
+// libnerf_b200.so -- the benchmark's reference arm -- renders the identical
+// datasets.
+#ifndef NB_SCENE_ENTRY
+#define NB_SCENE_ENTRY nerf_b200_scene_render
+#endif
+
 namespace {
 
 uint64_t mix64(uint64_t z) {
@@ -313,7 +321,7 @@ void camera_eye(const NerfB200SceneDesc& s, uint32_t view, double eye[3]) {
 
 extern "C" {
 
-NERF_API NerfStatus nerf_b200_scene_render(const NerfB200SceneDesc* s, uint8_t* images, float* cams, float* intrinsics) {
+NERF_API NerfStatus NB_SCENE_ENTRY(const NerfB200SceneDesc* s, uint8_t* images, float* cams, float* intrinsics) {
     if (!s || !cams || !intrinsics || s->width == 0u || s->height == 0u || !(s->fov > 0.0f)) return NERF_STATUS_INVALID_USAGE;
     const Scene sc = make_scene(*s);
     const uint32_t W = s->width, H = s->height;

@@ -45,7 +45,16 @@ class BatchInfo(C.Structure):
     _fields_ = [("rays", U32), ("active_rays", U32), ("samples", U32), ("camera", U32)]
 
 
+class SceneDesc(C.Structure):
+    """Mirror of NerfB200SceneDesc (include/nerf_b200.h): the synthetic-scene renderer's description."""
+    _fields_ = [("kind", U32), ("seed", U32), ("n_primitives", U32), ("density", F32), ("extent", F32),
+                ("size_min", F32), ("size_max", F32), ("n_views", U32), ("width", U32), ("height", U32), ("fov", F32),
+                ("radius", F32), ("camera_mode", U32), ("orbit_elevation", F32), ("orbit_views", U32),
+                ("view_offset", U32), ("n_threads", U32)]
+
+
 _PROTOS = {
+    "oracle_scene_render": (C.c_int, [C.POINTER(SceneDesc), P, P, P]),
     "oracle_hash_u32": (U32, [U32]),
     "oracle_rand01": (F32, [U32]),
     "oracle_train_camera": (U32, [U32, U32]),
@@ -107,6 +116,22 @@ def lib():
 
 def ptr(a):
     return None if a is None else a.ctypes.data
+
+
+def make_scene(kind=0, seed=0, n_primitives=3, density=50.0, extent=0.5, size_min=0.15, size_max=0.35, n_views=16,
+               width=128, height=128, fov=0.69, radius=3.0, camera_mode=0, orbit_elevation=0.5, orbit_views=0,
+               view_offset=0, n_threads=0, with_images=True):
+    """The seeded synthetic scenes and their exact renders, from this library's copy of the scene renderer (the same
+    source as nerf_b200_scene_render).  Returns (images [n,H,W,4] uint8, cameras [n,4,4] float32, (fx, fy, cx, cy))."""
+    d = SceneDesc(kind, seed, n_primitives, density, extent, size_min, size_max, n_views, width, height, fov, radius,
+                  camera_mode, orbit_elevation, orbit_views or n_views, view_offset, n_threads)
+    imgs = np.zeros((n_views, height, width, 4), np.uint8)
+    cams = np.zeros((n_views, 4, 4), np.float32)
+    intr = np.zeros(4, np.float32)
+    rc = lib().oracle_scene_render(C.byref(d), ptr(imgs) if with_images else None, ptr(cams), ptr(intr))
+    if rc != 0:
+        raise ValueError(f"oracle_scene_render failed with status {rc}")
+    return imgs, cams, tuple(float(x) for x in intr)
 
 
 def grid_layout(n_levels=16, log2_hashmap_size=19, base_resolution=16, max_resolution=2048) -> GridLayout:

@@ -165,11 +165,11 @@ def run(pretrain=2000, steps=200, render_views=4, render_spp=256, psnr_views=5, 
     """Config-2 training (the reference's limits: 128 steps per ray here, white background) and the config-3 render,
     both through the reference backend's nerf.h."""
     import bench  # the config-2 workload definition (dataset, training configuration)
-    import nerf_b200 as nb
+    import nerf_b200 as nb  # ctypes structures and the Dataset container; the product library is never loaded
 
     lib = load()
     out = {"library": "oracle/_ref/libref_stock.so (reference backend-cuda.cu, unchanged kernels, sm_100a)"}
-    ds, _ = bench.make_dataset(nb)
+    ds, _ = bench.make_dataset(nb, renderer=bench.oracle_scene)
     cfg = reference_train_config(nb, bench, max_steps_per_ray)
     rays = cfg.rays_per_batch
     t0 = time.perf_counter()
@@ -204,7 +204,7 @@ def run(pretrain=2000, steps=200, render_views=4, render_spp=256, psnr_views=5, 
 def heldout_psnr(lib, ctx, nb, bench, n, spp):
     """PSNR of the trained reference model on held-out views (the same cameras and ground truth as bench.py's
     psnr_heldout): weights saved, loaded into a context whose dataset cameras are the held-out views."""
-    held = nb.make_scene(**{**bench.CFG2, "n_views": n, "view_offset": bench.CFG2["n_views"],
+    held = bench.oracle_scene(**{**bench.CFG2, "n_views": n, "view_offset": bench.CFG2["n_views"],
                             "orbit_views": bench.CFG2["n_views"] + n})
     with tempfile.TemporaryDirectory() as d:
         path = pathlib.Path(d) / "ref.ckpt"
@@ -240,7 +240,7 @@ def render_config(nb, bench):
 def render_config3(lib, nb, bench, views, spp):
     """Config 3 through the reference: orbit poses passed as the dataset cameras (dummy images), the reference's
     seeded initial weights, uniform samples (the reference renders without the occupancy grid)."""
-    orbit = nb.make_scene(**{**bench.CFG2, "n_views": views, "camera_mode": 2, "orbit_elevation": 0.35,
+    orbit = bench.oracle_scene(**{**bench.CFG2, "n_views": views, "camera_mode": 2, "orbit_elevation": 0.35,
                              "orbit_views": 200, "view_offset": 0}, with_images=False)
     rc = RefContext(lib, orbit, bench.GRID_RES, RENDER_ROWS, 1 << 16)
     rc.configure(render_config(nb, bench))
@@ -259,7 +259,7 @@ def probe_configs():
     import bench
     import nerf_b200 as nb
     lib = load()
-    ds, _ = bench.make_dataset(nb)
+    ds, _ = bench.make_dataset(nb, renderer=bench.oracle_scene)
     res = []
     shapes = [tuple(int(x) for x in s.split(",")) for s in os.environ.get(
         "REF_PROBE_SHAPES", "4096,64,65536,1,32;4096,128,65536,1,32;4096,64,2097152,16,256;4096,128,2097152,16,256").split(";")]

@@ -5,12 +5,16 @@ inside a host application that owns the device memory budget, or code in
 which a cudaMalloc would synchronise the device at a bad moment.  For them
 the library offers a variant of nerf_b200_field_backward whose weight-gradient
 scratch lives in a static device array instead of a caller-allocated buffer.
-This test calls that variant twice in a row through the C ABI, with different
-upstream gradients, and checks each call against nerf_b200_field_backward
-with its own scratch on the same inputs: the MLP weight gradients must be
-identical (same kernel, same CTA count, same reduction order) and the
+This test calls that variant several times in a row through the C ABI, with
+different upstream gradients and then fewer rows (2500, 2500, 37, 0), and
+checks each call against nerf_b200_field_backward with its own scratch on
+the same inputs: the MLP weight gradients must be identical (same kernel,
+same CTA count, same reduction order), so rows of the shared array left over
+from a larger earlier call never leak into a smaller later one, and the
 hash-table gradients, summed with fp16 reductions in nondeterministic order,
 must agree within the relative L2 tolerance used by the other backward tests.
+The first call's gradients are also compared with the CPU oracle's field
+backward within the tolerances of the other field-backward tests.
 The file name sorts last so that a run stopping at the first failure has
 already run every other test.
 """
@@ -45,23 +49,33 @@ def test_field_backward_noalloc_matches_allocating_entry_point(cuda):
     feat = oracle.grid_forward(og, params[:n_grid], pos)
     assert lib.nerf_b200_field_backward_noalloc_max_rows() >= lib.nerf_b200_field_backward_partial_floats() // 10240
     par_d, pos_d, dir_d, feat_d = dev(torch, params), dev(torch, pos), dev(torch, dirs), dev(torch, feat)
-    for call in range(2):
-        dout = (rng.standard_normal((n, 4)) * (0.5 + call)).astype(np.float32)
+    for call, rows in enumerate((n, n, 37, 0)):
+        dout = np.zeros((n, 4), np.float32)
+        dout[:rows] = rng.standard_normal((rows, 4)) * (0.5 + call)
         dout_d = dev(torch, dout)
         gg_ref, mg_ref = zeros(torch, n_grid, np.uint16), zeros(torch, 10240, np.float32)
         part = zeros(torch, int(lib.nerf_b200_field_backward_partial_floats()), np.float32)
         check("field_backward", lib.nerf_b200_field_backward(
-            C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), n, feat_d.data_ptr(), dout_d.data_ptr(),
+            C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), rows, feat_d.data_ptr(), dout_d.data_ptr(),
             gg_ref.data_ptr(), part.data_ptr(), mg_ref.data_ptr(), None))
         gg, mg = zeros(torch, n_grid, np.uint16), zeros(torch, 10240, np.float32)
         check("field_backward_noalloc", lib.nerf_b200_field_backward_noalloc(
-            C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), n, feat_d.data_ptr(), dout_d.data_ptr(),
+            C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), rows, feat_d.data_ptr(), dout_d.data_ptr(),
             gg.data_ptr(), mg.data_ptr(), None))
         torch.cuda.synchronize()
         assert np.array_equal(host(mg), host(mg_ref)), call
         a = host(gg, np.uint16).view(np.float16).astype(np.float64)
         b = host(gg_ref, np.uint16).view(np.float16).astype(np.float64)
+        if rows == 0:
+            assert not host(mg).any() and not a.any() and not b.any()
+            continue
         assert np.linalg.norm(a - b) / np.linalg.norm(b) < 2e-2, call
+        if call == 0:
+            dfeat, wg = oracle.mlp_backward(params[n_grid:], feat[:rows], dirs[:rows], dout[:rows])
+            got_w = host(mg).astype(np.float64)
+            assert np.linalg.norm(got_w - wg) / np.linalg.norm(wg) < 1e-2
+            want_g = oracle.grid_backward(og, pos[:rows], dfeat)
+            assert np.linalg.norm(a - want_g) / np.linalg.norm(want_g) < 2e-2
     bad = lib.nerf_b200_field_backward_noalloc(C.byref(g), par_d.data_ptr(), pos_d.data_ptr(), dir_d.data_ptr(), 1 << 31,
                                                feat_d.data_ptr(), dout_d.data_ptr(), gg.data_ptr(), mg.data_ptr(), None)
     assert bad == abi.NERF_STATUS_INVALID_USAGE
