@@ -148,6 +148,19 @@ NERF_API NerfStatus nerf_b200_read_batch(void* context, uint32_t* ray_counts, ui
 NERF_API NerfStatus nerf_b200_dp_unique_id(uint8_t out_id[NERF_B200_DP_ID_BYTES]);
 NERF_API NerfStatus nerf_b200_dp_init(void* context, uint32_t rank, uint32_t world_size,
                                       const uint8_t id[NERF_B200_DP_ID_BYTES]);
+/* The failure path of a stalled rank, on one GPU.  In peer mode every wait
+ * of the step's barriers is bounded (NERF_B200_DP_TIMEOUT_MS, read by
+ * nerf_b200_dp_init; default 5000): a rank whose peer stops stepping gives up
+ * the wait, records the error, finishes its step, and nerf_read_train_stats
+ * returns NERF_STATUS_CUDA_ERROR from then on (the replicas are no longer in
+ * step).  This call runs the same barrier kernel on a configured
+ * single-GPU context (NERF_STATUS_STATE_ERROR otherwise) as rank 0 of two,
+ * against a second rank whose flag is never written, with a wait limit of
+ * timeout_us microseconds; asynchronous on the context's stream.  No
+ * counterpart in the reference, which has no multi-GPU path; its own failure
+ * report is the non-finite flag of the step statistics
+ * (backend-cuda.cu:1495-1508). */
+NERF_API NerfStatus nerf_b200_dp_barrier_test(void* context, uint32_t timeout_us);
 
 /* ------------------------------------------------------------- rendering */
 /* Render an arbitrary pose (row-major 3x4 camera-to-world, camera looks down

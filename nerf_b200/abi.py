@@ -276,6 +276,7 @@ B200_EXPORTS = {
     "nerf_b200_read_batch": (S, [P, P, P, P, P, P]),
     "nerf_b200_dp_unique_id": (S, [P]),
     "nerf_b200_dp_init": (S, [P, U32, U32, P]),
+    "nerf_b200_dp_barrier_test": (S, [P, U32]),
     "nerf_b200_render": (S, [P, C.POINTER(NerfB200RenderRequest), C.POINTER(NerfB200RenderInfo)]),
     "nerf_b200_render_output": (S, [P, C.POINTER(P)]),
     "nerf_b200_scene_render": (S, [C.POINTER(NerfB200SceneDesc), P, P, P]),

@@ -261,6 +261,12 @@ struct Context {
     unsigned char* peer_model[kMaxDpWorld] = {};
     float* dp_gsum = nullptr;   // owned range of summed gradients
     DpSync* dp_sync = nullptr;  // this rank's synchronisation words (model arena)
+    // Wait limit of the barriers (NERF_B200_DP_TIMEOUT_MS, default 5 s); dp_watch:
+    // nerf_read_train_stats reports a barrier that ran out (peer mode, or after
+    // nerf_b200_dp_barrier_test); dp_absent: the never-written rank of that test.
+    uint64_t dp_timeout_ns = 5000000000ull;
+    bool dp_watch = false;
+    DpSync* dp_absent = nullptr;
     float* mlp_sum = nullptr;   // MLP gradients + loss summed over the ranks (model arena)
     DpPeers dp_peers() const;
     uint64_t dp_lo(uint32_t r) const { return (n_grid / 8u) * r / dp_world * 8u; }
@@ -297,6 +303,8 @@ struct Context {
         dp_peer = false;
         if (comm && g_nccl.loaded) g_nccl.comm_destroy(comm);
         comm = nullptr;
+        if (dp_absent) cudaFree(dp_absent);
+        dp_absent = nullptr;
         if (stream) cudaStreamDestroy(stream);
         stream = nullptr;
         if (stats_host) cudaFreeHost(stats_host);
@@ -826,6 +834,7 @@ DpPeers Context::dp_peers() const {
     }
     d.gsum = dp_gsum;
     d.mlp_sum = mlp_sum;
+    d.timeout_ns = dp_timeout_ns;
     return d;
 }
 
@@ -1170,7 +1179,7 @@ NERF_API NerfStatus nerf_read_train_stats(void* context, NerfTrainStats* out) {
     const bool mirror = c->stats_host_current;
     if (!mirror) NB_TRY(cudaMemcpyAsync(out, &c->state->stats, sizeof(NerfTrainStats), cudaMemcpyDeviceToHost, c->stream));
     uint32_t dp_error = 0u, mlp_error = 0u;
-    if (c->dp_peer) NB_TRY(cudaMemcpyAsync(&dp_error, &c->dp_sync->error, 4, cudaMemcpyDeviceToHost, c->stream));
+    if (c->dp_peer || c->dp_watch) NB_TRY(cudaMemcpyAsync(&dp_error, &c->dp_sync->error, 4, cudaMemcpyDeviceToHost, c->stream));
     if (c->mlp_tc) NB_TRY(cudaMemcpyAsync(&mlp_error, &c->state->mlp_error, 4, cudaMemcpyDeviceToHost, c->stream));
     NB_TRY(cudaStreamSynchronize(c->stream));
     if (mirror) {
@@ -1571,6 +1580,10 @@ NERF_API NerfStatus nerf_b200_dp_init(void* context, uint32_t rank, uint32_t wor
     if (c->comm) return NERF_STATUS_STATE_ERROR;
     c->dp_rank = rank;
     c->dp_world = world;
+    if (const char* t = std::getenv("NERF_B200_DP_TIMEOUT_MS")) {
+        const double ms = std::atof(t);
+        if (ms > 0.0) c->dp_timeout_ns = static_cast<uint64_t>(ms * 1e6);
+    }
     if (world == 1u) return NERF_STATUS_OK;
     {
         std::lock_guard<std::mutex> lk2(nb::g_nccl_mu);
@@ -1586,6 +1599,29 @@ NERF_API NerfStatus nerf_b200_dp_init(void* context, uint32_t rank, uint32_t wor
     if (ps != NERF_STATUS_OK) return ps;
     c->configured = false;  // the step graph must be recaptured with the exchange
     return NERF_STATUS_OK;
+}
+
+NERF_API NerfStatus nerf_b200_dp_barrier_test(void* context, uint32_t timeout_us) {
+    if (!context || timeout_us == 0u) return NERF_STATUS_INVALID_USAGE;
+    Context* c = as_ctx(context);
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (!c->configured) return NERF_STATUS_STATE_ERROR;
+    if (c->comm) return NERF_STATUS_STATE_ERROR;  // only on a context that trains alone
+    if (!c->dp_absent) {
+        if (cudaMalloc(&c->dp_absent, sizeof(nb::DpSync)) != cudaSuccess) {
+            c->dp_absent = nullptr;
+            return NERF_STATUS_FAILURE;
+        }
+        NB_TRY(cudaMemsetAsync(c->dp_absent, 0, sizeof(nb::DpSync), c->stream));
+    }
+    nb::DpPeers d{};
+    d.world = 2u;
+    d.rank = 0u;
+    d.sync[0] = c->dp_sync;
+    d.sync[1] = c->dp_absent;  // rank 1 never announces an epoch
+    d.timeout_ns = static_cast<uint64_t>(timeout_us) * 1000u;
+    c->dp_watch = true;
+    return nb::cuda_status(nb::launch_dp_barrier(d, c->stream));
 }
 
 NERF_API NerfStatus nerf_b200_render(void* context, const NerfB200RenderRequest* r, NerfB200RenderInfo* info) {

@@ -182,6 +182,7 @@ struct DpPeers {
     DpSync* sync[kMaxDpWorld];          // every rank's synchronisation words
     float* gsum;                        // [hi - lo] summed gradients of the owned range
     float* mlp_sum;                     // [kMlpGradSlots] summed MLP gradients and loss
+    uint64_t timeout_ns;                // a barrier wait gives up after this long (DpSync::error)
 };
 struct OptimArgs {
     TrainConsts tc;
@@ -217,7 +218,7 @@ cudaError_t launch_splitmix_fill(float* dst, uint64_t n, uint64_t state0, float 
 // and non-finite flag go to every rank's DpSync::partials.
 cudaError_t launch_dp_reduce_grads(const OptimArgs& a, cudaStream_t s);
 // Barrier of all ranks over their DpSync words: each rank announces a new
-// epoch to every rank and waits (at most five seconds, then DpSync::error) until
+// epoch to every rank and waits (at most d.timeout_ns, then DpSync::error) until
 // every rank has announced it.  Writes made before it (by this rank's earlier
 // kernels, to any rank's memory) are visible to every rank after it.
 cudaError_t launch_dp_barrier(const DpPeers& d, cudaStream_t s);

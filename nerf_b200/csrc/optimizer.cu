@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(32) k_dp_barrier(const DpPeers d) {
             uint32_t seen;
             asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(seen) : "l"(&me->flags[t]) : "memory");
             if (static_cast<int32_t>(seen - epoch) >= 0) break;
-            if (global_ns() - t0 > 5000000000ull) {  // five seconds: give up, report, go on
+            if (global_ns() - t0 > d.timeout_ns) {  // give up, report, go on
                 atomicExch(&me->error, 1u);
                 break;
             }
