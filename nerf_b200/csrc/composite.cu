@@ -36,6 +36,11 @@ __device__ __forceinline__ float sigmoidf(float x) { return __fdiv_rn(1.0f, __fa
 __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a) {
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t k = blockIdx.x * kWarps + warp;
+    // Data parallel: this rank's sample count rides with the loss in the
+    // exchanged MLP-gradient buffer, so every rank sizes its next batch from
+    // the same global count (exact in fp32 below 2^24).
+    if (!a.direct && a.dp_world > 1u && blockIdx.x == 0u && threadIdx.x == 0u)
+        a.loss_slot[kMlpGradSamples - kMlpGradLoss] = static_cast<float>(a.state->n_samples);
     uint32_t n;
     float inv_norm;
     if (a.direct) {

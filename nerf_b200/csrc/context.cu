@@ -697,6 +697,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     op.n_params = n_params;
     op.stats_blocks = grad_stats_blocks(n_params);
     op.mlp_in = mlp_grad;
+    op.world = dp_world;
     if (dp_peer) {
         op.dp_peer = 1u;
         op.dp = dp_peers();

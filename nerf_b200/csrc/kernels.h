@@ -204,6 +204,7 @@ struct OptimArgs {
     const float* mlp_in;         // MLP gradients + loss read by statistics and Adam (mlp_grad, or dp.mlp_sum)
     uint32_t fuse_wgrad;         // statistics kernel also reduces the weight-gradient partials (single GPU)
     StatsBlock* stats_host;      // mapped pinned host mirror of the step statistics, or null
+    uint32_t world;              // data-parallel ranks (1: one GPU)
 };
 cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);

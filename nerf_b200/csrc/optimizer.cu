@@ -197,8 +197,15 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
     st->total_samples += samples;
     st->total_rays += rays;
     if (tc.target_samples != 0u) {
-        unsigned long long next = samples == 0u ? 2ull * rays
-                                                : static_cast<unsigned long long>(rays) * tc.target_samples / samples;
+        // Data parallel: every rank marches the same number of rays, sized from
+        // the samples of all ranks against the target of all ranks, so that no
+        // rank's batch drifts from the others' and the barriers wait less.
+        unsigned long long tot = samples, tgt = tc.target_samples;
+        if (a.world > 1u) {
+            tot = static_cast<unsigned long long>(*reinterpret_cast<volatile const float*>(a.mlp_in + kMlpGradSamples));
+            tgt *= a.world;
+        }
+        unsigned long long next = tot == 0u ? 2ull * rays : static_cast<unsigned long long>(rays) * tgt / tot;
         next = next < 128ull ? 128ull : next;
         next = next > tc.max_rays ? tc.max_rays : next;
         st->n_rays = static_cast<uint32_t>(next);

@@ -31,6 +31,7 @@ constexpr uint32_t kMlpParams = kMlpC2 + 16 * 64;  // 10240
 // The fp32 MLP-gradient buffer carries extra scalars after the weights so
 // that one data-parallel all-reduce sums them with the gradients.
 constexpr uint32_t kMlpGradLoss = kMlpParams;      // sum of normalised ray losses
+constexpr uint32_t kMlpGradSamples = kMlpParams + 1;  // this step's compacted samples (summed over the ranks)
 constexpr uint32_t kMlpGradSlots = kMlpParams + 8;
 
 constexpr uint32_t kOccNone = 0, kOccWarmupInit = 1, kOccRefresh = 2;

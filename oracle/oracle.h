@@ -154,6 +154,10 @@ uint64_t oracle_ctx_param_count(void* ctx, uint64_t* n_grid, uint64_t* n_mlp);
 int oracle_ctx_get_params(void* ctx, float* master, uint16_t* p16, float* m, float* v, float* grad);
 int oracle_ctx_set_params(void* ctx, const float* master);
 int oracle_ctx_set_grads(void* ctx, const float* grad, float loss_sum, uint32_t active_rays);
+// Data parallel with a per-step sample target: the compacted samples of all
+// ranks in the pending step (call between step_grads and step_apply); the
+// next ray count then follows the global count against world x target.
+int oracle_ctx_set_global_samples(void* ctx, uint64_t samples);
 /* World positions (x, y, z) of the update_count cells queried by an
  * occupancy refresh at this frame. */
 void oracle_occupancy_cells(uint32_t frame, uint32_t update_count, uint32_t cell_count, uint32_t grid_res, const float* mn,

@@ -84,6 +84,7 @@ _PROTOS = {
     "oracle_ctx_get_params": (C.c_int, [P, P, P, P, P, P]),
     "oracle_ctx_set_params": (C.c_int, [P, P]),
     "oracle_ctx_set_grads": (C.c_int, [P, P, F32, U32]),
+    "oracle_ctx_set_global_samples": (C.c_int, [P, U64]),
     "oracle_ctx_get_loss": (C.c_int, [P, P, P]),
     "oracle_occupancy_cells": (None, [U32, U32, U32, U32, P, P, P]),
     "oracle_ctx_get_occupancy": (C.c_int, [P, P, P]),
@@ -304,6 +305,10 @@ class Context:
     def set_grads(self, grad, loss_sum, active):
         grad = np.ascontiguousarray(grad, np.float32)
         self.lib.oracle_ctx_set_grads(self.h, ptr(grad), loss_sum, active)
+
+    def set_global_samples(self, samples):
+        """Data parallel: the pending step's compacted samples summed over all ranks."""
+        self.lib.oracle_ctx_set_global_samples(self.h, int(samples))
 
     def loss(self):
         """(normalised loss sum, kept rays) of the pending step."""

@@ -201,6 +201,9 @@ struct Ctx {
     uint32_t frame = 0, n_rays = 0;
     NerfTrainStats stats{};
     double loss_sum = 0.0;
+    // Data parallel: the compacted samples of all ranks in this step (set by
+    // the caller with the summed gradients; 0: this rank's own count).
+    uint64_t global_samples = 0;
     uint32_t active = 0;
     bool grads_pending = false;
     // last batch
@@ -516,14 +519,21 @@ void Ctx::apply_update() {
                    cfg.hyper_params.adam_beta2, cfg.hyper_params.adam_eps, s);
     });
     // Next step's ray count when a per-step sample target is set.
+    // Data parallel: every rank sizes its next batch from the samples of all
+    // ranks against the target of all ranks, so all ranks march the same count.
     if (opt.target_samples_per_step != 0u) {
-        const uint64_t samples = info.samples;
-        uint64_t next = samples == 0u ? 2ull * n_rays : static_cast<uint64_t>(n_rays) * opt.target_samples_per_step / samples;
+        uint64_t samples = info.samples, target = opt.target_samples_per_step;
+        if (opt.dp_world > 1u && global_samples != 0u) {
+            samples = global_samples;
+            target *= opt.dp_world;
+        }
+        uint64_t next = samples == 0u ? 2ull * n_rays : static_cast<uint64_t>(n_rays) * target / samples;
         next = std::max<uint64_t>(128u, std::min<uint64_t>(next, max_batch_rays));
         n_rays = static_cast<uint32_t>(next);
     }
     ++frame;
     grads_pending = false;
+    global_samples = 0;
 }
 
 }  // namespace oracle
@@ -670,6 +680,11 @@ int oracle_ctx_set_grads(void* ctx, const float* grad, float loss_sum, uint32_t 
     std::memcpy(c->grad.data(), grad, c->n_params * 4);
     c->loss_sum = loss_sum;
     c->active = active_rays;
+    return NERF_STATUS_OK;
+}
+
+int oracle_ctx_set_global_samples(void* ctx, uint64_t samples) {
+    static_cast<Ctx*>(ctx)->global_samples = samples;
     return NERF_STATUS_OK;
 }
 

@@ -22,22 +22,24 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("peer", ["1", "0"])
-@pytest.mark.parametrize("steps", [1, 3])
-def test_two_gpu_training_matches_oracle(peer, steps):
+@pytest.mark.parametrize("peer,steps,target", [("1", 1, 0), ("1", 3, 0), ("0", 1, 0), ("0", 3, 0),
+                                               ("1", 3, dp_worker.TARGET), ("0", 3, dp_worker.TARGET)])
+def test_two_gpu_training_matches_oracle(peer, steps, target):
+    """target > 0: both ranks size every batch from the samples of both (the same ray count on both ranks)."""
     old = os.environ.get("NERF_B200_DP_PEER")
     os.environ["NERF_B200_DP_PEER"] = peer
     try:
-        res = _run(dp_worker.gpu_rank, 2, steps)
+        res = _run(dp_worker.gpu_rank, 2, steps, target)
     finally:
         if old is None:
             del os.environ["NERF_B200_DP_PEER"]
         else:
             os.environ["NERF_B200_DP_PEER"] = old
-    (g0, m0, c0, l0), (g1, m1, c1, l1) = res[0], res[1]
+    (g0, m0, c0, l0, r0), (g1, m1, c1, l1, r1) = res[0], res[1]
     assert np.array_equal(g0, g1) and np.array_equal(m0, m1), "replicas diverged"
     assert l0 == l1
-    _, batches, params = dp_worker.serial_emulation(2, steps)
+    assert r0 == r1
+    _, batches, params = dp_worker.serial_emulation(2, steps, target)
     assert np.array_equal(batches[0]["counts"], c0)
     assert np.array_equal(batches[1]["counts"], c1)
     om = params[0][2]
