@@ -214,17 +214,11 @@ def run_ours(args):
 
     lib = abi.load()
     ds, gen_s = make_dataset(nb, args.views)
-    pinned_imgs = torch.from_numpy(ds.images).pin_memory()  # host buffer of the e2e job
-    ds_pinned = nb.Dataset(pinned_imgs.numpy(), ds.cameras, ds.intrinsics)
 
     ctx = nb.Context(ds, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
                      options=options(nb))
-    uid = None
     if world > 1:
-        obj = [nb.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        uid = obj[0]
-        ctx.dp_init(rank, world, uid)
+        dp_setup(nb, ctx, rank, world)
     ctx.configure(train_config(nb))
     sp = C.c_void_p()
     abi.check("stream", lib.nerf_b200_context_stream(ctx.handle, C.byref(sp)))
@@ -292,7 +286,9 @@ def run_ours(args):
     if not args.skip_e2e:
         ctx.close()
         torch.cuda.synchronize()
-        e2e = run_e2e(nb, lib, ds_pinned, rank, world, uid, args)
+        pinned_imgs = torch.from_numpy(ds.images).pin_memory()  # host buffer of the e2e job
+        ds_pinned = nb.Dataset(pinned_imgs.numpy(), ds.cameras, ds.intrinsics)
+        e2e = run_e2e(nb, lib, ds_pinned, rank, world, args)
 
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:  # the CPU baseline: rank 0 at N = 1 only
@@ -568,23 +564,37 @@ def run_render(nb, ctx, rank, world, args):
             "device_ms": ms, "wall_s": wall, "tiles": "64x64 round-robin over ranks"}
 
 
-def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
-    """Whole job through the C ABI with host buffers: create (uploads the pinned images), configure, and each step
-    nerf_train_step + nerf_read_train_stats.  Samples come from the additive counters export."""
+def dp_setup(nb, ctx, rank, world):
+    """Data-parallel set-up of a context.  Peer mode (default): the ranks' peer handles are all-gathered over the
+    job's own process group and mapped (nerf_b200_dp_init_peers; no NCCL communicator of the library's own).
+    NERF_B200_DP_PEER=0: the NCCL all-reduce path (nerf_b200_dp_init with a fresh NCCL id)."""
+    import torch.distributed as dist
+    if os.environ.get("NERF_B200_DP_PEER", "1") == "0":
+        obj = [nb.dp_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx.dp_init(rank, world, obj[0])
+        return
+    handles = [None] * world
+    dist.all_gather_object(handles, ctx.dp_peer_handle())
+    ctx.dp_init_peers(rank, world, handles)
+
+
+def run_e2e(nb, lib, ds_pinned, rank, world, args):
+    """Whole job through the C ABI with host buffers: create (uploads the pinned images), data-parallel set-up,
+    configure, and each step nerf_train_step + nerf_read_train_stats.  Samples come from the additive counters
+    export."""
     import torch
     import torch.distributed as dist
     steps = args.e2e_steps
-    if world > 1:  # a fresh communicator for this job: NCCL ids are single-use
-        obj = [nb.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(obj, src=0)
-        uid = obj[0]
+    if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     ctx = nb.Context(ds_pinned, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
                      options=options(nb))
+    t_upload = time.perf_counter()
     if world > 1:
-        ctx.dp_init(rank, world, uid)
+        dp_setup(nb, ctx, rank, world)
     t_create = time.perf_counter()
     ctx.configure(train_config(nb))
     t_configure = time.perf_counter()
@@ -605,10 +615,12 @@ def run_e2e(nb, lib, ds_pinned, rank, world, uid, args):
         secs, samples = float(t[0]), float(t[1])
     h2d = ds_pinned.images.nbytes + ds_pinned.cameras.nbytes
     return {"value": samples / secs, "unit": "samples/s", "steps": steps, "seconds": secs,
-            "phases_s": {"create_upload": t_create - t0, "configure": t_configure - t_create, "steps": t1 - t_configure},
+            "create_upload_s": t_upload - t0, "dp_setup_s": t_create - t_upload, "configure_s": t_configure - t_create,
+            "steps_s": t1 - t_configure,
             "h2d_bytes_per_step": h2d / steps, "d2h_bytes_per_step": 20,
-            "note": "create+upload, configure and every step train_step + read_train_stats, wall clock, max over ranks; "
-                    "includes the occupancy warm-up phase of a fresh job"}
+            "note": "create+upload, data-parallel set-up (peer handles all-gathered and mapped), configure and every "
+                    "step train_step + read_train_stats, wall clock on each rank (the phases: rank 0's), max over "
+                    "ranks; includes the occupancy warm-up phase of a fresh job"}
 
 
 def dataset_io(lib, ds):

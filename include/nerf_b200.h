@@ -148,6 +148,21 @@ NERF_API NerfStatus nerf_b200_read_batch(void* context, uint32_t* ray_counts, ui
 NERF_API NerfStatus nerf_b200_dp_unique_id(uint8_t out_id[NERF_B200_DP_ID_BYTES]);
 NERF_API NerfStatus nerf_b200_dp_init(void* context, uint32_t rank, uint32_t world_size,
                                       const uint8_t id[NERF_B200_DP_ID_BYTES]);
+/* Peer mode without NCCL: every rank exports its handle (the CUDA IPC
+ * handle of its model memory plus the sizes all ranks must share), the caller
+ * gathers the world's handles in rank order with any host-side exchange it
+ * already has (a torch.distributed all-gather, an MPI all-gather, a file), and
+ * every rank passes the gathered array (world x NERF_B200_DP_HANDLE_BYTES) to
+ * nerf_b200_dp_init_peers before nerf_configure_training.  The step is the
+ * same peer-mode step as after nerf_b200_dp_init, but no communicator is
+ * created, so setting up a job costs a few IPC mappings instead of an NCCL
+ * initialisation.  Errors: INVALID_USAGE for a handle of another layout or
+ * world > 64; STATE_ERROR when the context is already data parallel; FAILURE
+ * when a peer's memory cannot be mapped (then nothing is mapped and the
+ * context stays single-GPU: the caller must not train the ranks apart). */
+#define NERF_B200_DP_HANDLE_BYTES 128
+NERF_API NerfStatus nerf_b200_dp_peer_handle(void* context, uint8_t out[NERF_B200_DP_HANDLE_BYTES]);
+NERF_API NerfStatus nerf_b200_dp_init_peers(void* context, uint32_t rank, uint32_t world_size, const uint8_t* handles);
 /* The failure path of a stalled rank, on one GPU.  In peer mode every wait
  * of the step's barriers is bounded (NERF_B200_DP_TIMEOUT_MS, read by
  * nerf_b200_dp_init; default 5000): a rank whose peer stops stepping gives up

@@ -224,6 +224,19 @@ class Context:
         return dict(counts=counts, index=index, dir=f[:, 0:3].copy(), begin=u[:, 3].copy(), gt=f[:, 4:8].copy(),
                     bg=f[:, 8:11].copy(), count=u[:, 11].copy(), pos_dt=pos, sample_ray=sray)
 
+    def dp_peer_handle(self) -> bytes:
+        """This rank's peer handle (nerf_b200_dp_peer_handle) for a host-side all-gather."""
+        buf = (C.c_uint8 * 128)()
+        check("nerf_b200_dp_peer_handle", self.lib.nerf_b200_dp_peer_handle(self.handle, buf))
+        return bytes(buf)
+
+    def dp_init_peers(self, rank: int, world: int, handles: list):
+        """Peer-mode data parallelism from the world's handles in rank order (nerf_b200_dp_init_peers): no NCCL."""
+        blob = b"".join(handles)
+        assert len(blob) == 128 * world
+        buf = (C.c_uint8 * len(blob)).from_buffer_copy(blob)
+        check("nerf_b200_dp_init_peers", self.lib.nerf_b200_dp_init_peers(self.handle, rank, world, buf))
+
     def dp_init(self, rank: int, world: int, uid: bytes):
         buf = (C.c_uint8 * 128).from_buffer_copy(uid)
         check("nerf_b200_dp_init", self.lib.nerf_b200_dp_init(self.handle, rank, world, buf))

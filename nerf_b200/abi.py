@@ -277,6 +277,8 @@ B200_EXPORTS = {
     "nerf_b200_dp_unique_id": (S, [P]),
     "nerf_b200_dp_init": (S, [P, U32, U32, P]),
     "nerf_b200_dp_barrier_test": (S, [P, U32]),
+    "nerf_b200_dp_peer_handle": (S, [P, P]),
+    "nerf_b200_dp_init_peers": (S, [P, U32, U32, P]),
     "nerf_b200_render": (S, [P, C.POINTER(NerfB200RenderRequest), C.POINTER(NerfB200RenderInfo)]),
     "nerf_b200_render_output": (S, [P, C.POINTER(P)]),
     "nerf_b200_scene_render": (S, [C.POINTER(NerfB200SceneDesc), P, P, P]),

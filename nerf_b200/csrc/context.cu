@@ -48,6 +48,10 @@ static_assert(sizeof(StatsBlock) == sizeof(NerfTrainStats), "stats mirror");
 
 constexpr uint32_t kMaxStepsPerRay = 4096;  // the reference allows 256
 constexpr int kStepKernels = 14;            // timed segments of one training step
+// Exported peer handle: the model arena's CUDA IPC handle, then the arena's
+// size and parameter count (all ranks' must agree), then a format word.
+constexpr uint32_t kDpHandleBytes = NERF_B200_DP_HANDLE_BYTES;
+constexpr uint32_t kDpHandleMagic = 0x4E42504Bu;
 
 // ---------------------------------------------------------------- helpers
 uint64_t align_up(uint64_t v, uint64_t a) { return (v + a - 1u) / a * a; }
@@ -275,6 +279,10 @@ struct Context {
         return reinterpret_cast<T*>(peer_model[r] + (reinterpret_cast<const unsigned char*>(local) - model.base));
     }
     NerfStatus open_peers();
+    // Maps the other ranks' model arenas from their exported handles (world x
+    // kDpHandleBytes); false when any cannot be opened (nothing stays mapped).
+    bool map_peers(const unsigned char* handles);
+    bool dp_active() const { return dp_world > 1u && (comm != nullptr || dp_peer); }
     // Host copy of a buffer of the model arena whose grid part is sharded over
     // the ranks in peer mode (masters, moments): each range from its owner.
     cudaError_t read_sharded(void* host, const float* local, uint64_t n) const;
@@ -734,11 +742,11 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     if ((e = mark()) != cudaSuccess) return e;
     if ((e = launch_grid_scatter(fa, s)) != cudaSuccess || (e = mark()) != cudaSuccess) return e;
     // One GPU: the statistics kernel also reduces the weight-gradient partials.
-    op.fuse_wgrad = comm ? 0u : 1u;
+    op.fuse_wgrad = dp_active() ? 0u : 1u;
     op.stats_host = stats_host_dev;
     if (!op.fuse_wgrad && (e = launch_wgrad_reduce(op, s)) != cudaSuccess) return e;
     if ((e = mark()) != cudaSuccess) return e;
-    if (comm && dp_peer) {
+    if (dp_peer) {
         // Peer mode, no collective library in the step: after a barrier (every
         // rank's gradients are complete) each rank sums its owned range of all
         // ranks' hash gradients and all ranks' MLP gradients over NVLink and
@@ -763,7 +771,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
         return e;
     // Peer mode: every rank wrote its owned fp16 parameters into every rank's
     // mirror; no rank reads them before all writes are done.
-    if (comm && dp_peer && (e = launch_dp_barrier(op.dp, s)) != cudaSuccess) return e;
+    if (dp_peer && (e = launch_dp_barrier(op.dp, s)) != cudaSuccess) return e;
     if ((e = mark()) != cudaSuccess) return e;
     return cudaSuccess;
 }
@@ -790,21 +798,9 @@ NerfStatus Context::open_peers() {
               cudaMemcpy(all.data(), dbuf, hb * dp_world, cudaMemcpyDeviceToHost) == cudaSuccess;
     bool opened = ok && want;
     if (opened) {
-        for (uint32_t r = 0; r < dp_world; ++r) {
-            if (r == dp_rank) {
-                peer_model[r] = model.base;
-                continue;
-            }
-            cudaIpcMemHandle_t h;
-            std::memcpy(&h, all.data() + hb * r, hb);
-            void* p = nullptr;
-            if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-                cudaGetLastError();
-                opened = false;
-                break;
-            }
-            peer_model[r] = static_cast<unsigned char*>(p);
-        }
+        std::vector<unsigned char> full(kDpHandleBytes * dp_world, 0);
+        for (uint32_t r = 0; r < dp_world; ++r) std::memcpy(full.data() + kDpHandleBytes * r, all.data() + hb * r, hb);
+        opened = map_peers(full.data());
     }
     const float f = opened ? 1.0f : 0.0f;
     float agreed = 0.0f;
@@ -819,6 +815,31 @@ NerfStatus Context::open_peers() {
         for (auto& p : peer_model) p = nullptr;
     }
     return ok ? NERF_STATUS_OK : NERF_STATUS_FAILURE;
+}
+
+bool Context::map_peers(const unsigned char* handles) {
+    bool opened = true;
+    for (uint32_t r = 0; r < dp_world && opened; ++r) {
+        if (r == dp_rank) {
+            peer_model[r] = model.base;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, handles + kDpHandleBytes * r, sizeof(h));
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            opened = false;
+            break;
+        }
+        peer_model[r] = static_cast<unsigned char*>(p);
+    }
+    if (!opened) {
+        for (uint32_t r = 0; r < kMaxDpWorld; ++r)
+            if (peer_model[r] && r != dp_rank) cudaIpcCloseMemHandle(peer_model[r]);
+        for (auto& p : peer_model) p = nullptr;
+    }
+    return opened;
 }
 
 DpPeers Context::dp_peers() const {
@@ -1463,7 +1484,7 @@ NERF_API NerfStatus nerf_b200_read_counters(void* context, NerfB200Counters* out
     // MLP backward + scatter, statistics, Adam (the tensor-core path splits the
     // forward into encode + MLP); data parallel adds the weight-gradient
     // reduction, and peer mode its barriers and gradient reduction.
-    out->kernels_per_step = 12u + (c->mlp_tc ? 1u : 0u) + (c->comm ? 1u : 0u) + (c->dp_peer ? 4u : 0u);
+    out->kernels_per_step = 12u + (c->mlp_tc ? 1u : 0u) + (c->dp_active() ? 1u : 0u) + (c->dp_peer ? 4u : 0u);
     out->dp_peer = c->dp_peer ? 1u : 0u;
     return NERF_STATUS_OK;
 }
@@ -1602,12 +1623,60 @@ NERF_API NerfStatus nerf_b200_dp_init(void* context, uint32_t rank, uint32_t wor
     return NERF_STATUS_OK;
 }
 
+NERF_API NerfStatus nerf_b200_dp_peer_handle(void* context, uint8_t out[NERF_B200_DP_HANDLE_BYTES]) {
+    if (!context || !out) return NERF_STATUS_INVALID_USAGE;
+    Context* c = as_ctx(context);
+    std::lock_guard<std::mutex> lk(c->mu);
+    cudaIpcMemHandle_t h{};
+    if (cudaIpcGetMemHandle(&h, c->model.base) != cudaSuccess) {
+        cudaGetLastError();
+        return NERF_STATUS_CUDA_ERROR;
+    }
+    std::memset(out, 0, NERF_B200_DP_HANDLE_BYTES);
+    std::memcpy(out, &h, sizeof(h));
+    const uint64_t meta[2] = {c->model.size, c->n_params};
+    std::memcpy(out + sizeof(h), meta, sizeof(meta));
+    std::memcpy(out + sizeof(h) + sizeof(meta), &nb::kDpHandleMagic, 4);
+    return NERF_STATUS_OK;
+}
+
+NERF_API NerfStatus nerf_b200_dp_init_peers(void* context, uint32_t rank, uint32_t world, const uint8_t* handles) {
+    static_assert(sizeof(cudaIpcMemHandle_t) + 20 <= NERF_B200_DP_HANDLE_BYTES, "handle layout");
+    if (!context || !handles || world < 2u || world > nb::kMaxDpWorld || rank >= world) return NERF_STATUS_INVALID_USAGE;
+    Context* c = as_ctx(context);
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (c->comm || c->dp_peer || c->dp_world != 1u) return NERF_STATUS_STATE_ERROR;
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    for (uint32_t r = 0; r < world; ++r) {  // every rank's arena has this rank's layout
+        const uint8_t* h = handles + static_cast<size_t>(NERF_B200_DP_HANDLE_BYTES) * r;
+        uint64_t meta[2];
+        uint32_t magic = 0;
+        std::memcpy(meta, h + hb, sizeof(meta));
+        std::memcpy(&magic, h + hb + sizeof(meta), 4);
+        if (magic != nb::kDpHandleMagic || meta[0] != c->model.size || meta[1] != c->n_params) return NERF_STATUS_INVALID_USAGE;
+    }
+    if (const char* t = std::getenv("NERF_B200_DP_TIMEOUT_MS")) {
+        const double ms = std::atof(t);
+        if (ms > 0.0) c->dp_timeout_ns = static_cast<uint64_t>(ms * 1e6);
+    }
+    c->dp_rank = rank;
+    c->dp_world = world;
+    if (!c->map_peers(handles)) {
+        c->dp_rank = 0u;
+        c->dp_world = 1u;
+        return NERF_STATUS_FAILURE;
+    }
+    c->dp_peer = true;
+    c->configured = false;  // the step graph must be recaptured with the exchange
+    return NERF_STATUS_OK;
+}
+
 NERF_API NerfStatus nerf_b200_dp_barrier_test(void* context, uint32_t timeout_us) {
     if (!context || timeout_us == 0u) return NERF_STATUS_INVALID_USAGE;
     Context* c = as_ctx(context);
     std::lock_guard<std::mutex> lk(c->mu);
     if (!c->configured) return NERF_STATUS_STATE_ERROR;
-    if (c->comm) return NERF_STATUS_STATE_ERROR;  // only on a context that trains alone
+    if (c->dp_active()) return NERF_STATUS_STATE_ERROR;  // only on a context that trains alone
     if (!c->dp_absent) {
         if (cudaMalloc(&c->dp_absent, sizeof(nb::DpSync)) != cudaSuccess) {
             c->dp_absent = nullptr;

@@ -89,8 +89,10 @@ def serial_emulation(world, steps, target=0):
     return [oc.params()[0] for oc in ocs], [oc.batch() for oc in ocs], [oc.params() for oc in ocs]
 
 
-def gpu_rank(rank, world, port, steps, q, target=0):
-    """One rank of GPU data-parallel training (NCCL inside the step)."""
+def gpu_rank(rank, world, port, steps, q, target=0, setup="nccl"):
+    """One rank of GPU data-parallel training.  setup "nccl": nerf_b200_dp_init (an NCCL communicator; peer mode
+    unless NERF_B200_DP_PEER=0); "handles": the ranks' peer handles all-gathered over gloo and mapped with
+    nerf_b200_dp_init_peers (peer mode, no NCCL)."""
     try:
         import torch
         import nerf_b200
@@ -100,10 +102,16 @@ def gpu_rank(rank, world, port, steps, q, target=0):
         ctx = nerf_b200.Context(ds, grid_res=RES, max_sample_steps=RAYS * STEPS, max_batch_rays=4 * RAYS,
                                 options=nerf_b200.default_options(log2_hashmap_size=LOG2T, max_resolution=MAXRES,
                                                                   target_samples_per_step=target))
-        uid = [nerf_b200.dp_unique_id() if rank == 0 else None]
-        dist.broadcast_object_list(uid, src=0)
-        ctx.dp_init(rank, world, uid[0])
+        if setup == "handles":
+            handles = [None] * world
+            dist.all_gather_object(handles, ctx.dp_peer_handle())
+            ctx.dp_init_peers(rank, world, handles)
+        else:
+            uid = [nerf_b200.dp_unique_id() if rank == 0 else None]
+            dist.broadcast_object_list(uid, src=0)
+            ctx.dp_init(rank, world, uid[0])
         ctx.configure(cfg)
+        assert ctx.counters().dp_peer == (0 if os.environ.get("NERF_B200_DP_PEER") == "0" and setup == "nccl" else 1)
         rays = []
         for _ in range(steps):
             ctx.train_step()

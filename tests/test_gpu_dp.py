@@ -1,7 +1,7 @@
 """Data-parallel GPU training (needs two GPUs; skipped otherwise).
 
-Two processes, one per GPU, train through nerf_b200_dp_init + nerf_train_step,
-in both exchange modes: peer mode (each rank sums its owned range of every
+Two processes, one per GPU, train through nerf_b200_dp_init (or
+nerf_b200_dp_init_peers) + nerf_train_step, in both exchange modes: peer mode (each rank sums its owned range of every
 rank's hash gradients over NVLink, runs Adam on it and writes the fp16
 parameters into every rank's mirror) and the NCCL all-reduce path
 (NERF_B200_DP_PEER=0).  Both replicas must be bitwise identical after every
@@ -22,14 +22,17 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("peer,steps,target", [("1", 1, 0), ("1", 3, 0), ("0", 1, 0), ("0", 3, 0),
-                                               ("1", 3, dp_worker.TARGET), ("0", 3, dp_worker.TARGET)])
-def test_two_gpu_training_matches_oracle(peer, steps, target):
-    """target > 0: both ranks size every batch from the samples of both (the same ray count on both ranks)."""
+@pytest.mark.parametrize("peer,steps,target,setup", [
+    ("1", 1, 0, "nccl"), ("1", 3, 0, "nccl"), ("0", 1, 0, "nccl"), ("0", 3, 0, "nccl"),
+    ("1", 3, dp_worker.TARGET, "nccl"), ("0", 3, dp_worker.TARGET, "nccl"),
+    ("1", 3, 0, "handles"), ("1", 3, dp_worker.TARGET, "handles")])
+def test_two_gpu_training_matches_oracle(peer, steps, target, setup):
+    """target > 0: both ranks size every batch from the samples of both (the same ray count on both ranks).
+    setup "handles": peer mode set up from all-gathered peer handles without NCCL (nerf_b200_dp_init_peers)."""
     old = os.environ.get("NERF_B200_DP_PEER")
     os.environ["NERF_B200_DP_PEER"] = peer
     try:
-        res = _run(dp_worker.gpu_rank, 2, steps, target)
+        res = _run(dp_worker.gpu_rank, 2, steps, target, setup)
     finally:
         if old is None:
             del os.environ["NERF_B200_DP_PEER"]
