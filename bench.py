@@ -224,12 +224,18 @@ def run_ours(args):
     abi.check("stream", lib.nerf_b200_context_stream(ctx.handle, C.byref(sp)))
     stream = torch.cuda.ExternalStream(sp.value)
 
+    def step():
+        if args.eager:  # the same kernels launched one by one (nerf_b200_train_step_profiled): no graph launches
+            abi.check("eager step", lib.nerf_b200_train_step_profiled(ctx.handle, C.byref(abi.NerfB200StepProfile())))
+        else:
+            ctx.train_step()
+
     clocks = ClockSampler(local)
     clocks.start()  # running well before the timed region
     for _ in range(args.pretrain):
-        ctx.train_step()
+        step()
     for _ in range(args.warmup):
-        ctx.train_step()
+        step()
     c0 = ctx.counters()
     if world > 1:
         dist.barrier()
@@ -238,7 +244,7 @@ def run_ours(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        ctx.train_step()
+        step()
     e1.record(stream)
     torch.cuda.synchronize()
     clocks.mark(h0, time.time())
@@ -477,7 +483,10 @@ def ctx_partials(ctx):
 def roofline(kernels):
     """The dominant kernel (longest mean time in the kernel-by-kernel step) against its own bound."""
     pk = measured_peaks()
-    dom = max((k for k in kernels if "frac" in k), key=lambda k: k["ms"])
+    timed = [k for k in kernels if "frac" in k]
+    if not timed:  # no kernel-by-kernel steps were run (--profile-steps 0)
+        return None
+    dom = max(timed, key=lambda k: k["ms"])
     src = {"hbm": f"MEASURED_PEAKS.json hbm_gbs ({pk['source']})",
            "tensor": f"MEASURED_PEAKS.json bf16_tflops_sustained ({pk['source']})",
            "l2_gather": "live probe: 4-byte loads at hashed addresses of an L2-resident 32 MB buffer",
@@ -921,6 +930,9 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 4],
                     help="2: bounded training (the headline); 4: the large unbounded-style scene with cascades")
     ap.add_argument("--micro", action="store_true", help="kernel microbench sweep (config 5) instead of the step")
+    ap.add_argument("--eager", action="store_true",
+                    help="launch every step kernel by kernel instead of as the captured graph (for profilers, which "
+                         "are slow on graph launches; the same kernels in the same order)")
     ap.add_argument("--micro-reps", type=int, default=10)
     ap.add_argument("--micro-points", type=int, nargs="*", default=[20, 22, 24])
     ap.add_argument("--micro-tables", type=int, nargs="*", default=[14, 19, 22, 24])

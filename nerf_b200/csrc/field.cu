@@ -331,29 +331,34 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
 // 2l+1).  Warp w takes levels w, w+4, w+8, w+12 and lane j rows j and j+32,
 // so one gather instruction reads one level for 32 consecutive rows: on all
 // but the finest levels consecutive samples of a ray (or neighbouring pixels
-// of a render tile) share cells, and their loads fall into few sectors.
-// ok(row, pos) says whether a row is live.
+// of a render tile) share cells, and their loads fall into few sectors.  Two
+// levels are looked up per round, so each lane has the loads of four
+// (row, level) lookups -- 16 to 32 loads -- in flight before it waits.
+// ok(row, pos) says whether a row is live; a dead row loads nothing and
+// stores zeros.
 template <class Ok>
 __device__ __forceinline__ void encode_rows(const uint32_t* __restrict__ P, const LevelParams* lv, uint32_t hash_mask,
                                             const float4* pos, __half* feat, Ok ok) {
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t ra = lane, rb = lane + 32u;
     const float4 pa4 = pos[ra], pb4 = pos[rb];
-    const float pa[3] = {pa4.x, pa4.y, pa4.z}, pb[3] = {pb4.x, pb4.y, pb4.z};
     const bool oka = ok(ra, pa4), okb = ok(rb, pb4);
+    const float pa[3] = {oka ? pa4.x : 0.0f, oka ? pa4.y : 0.0f, oka ? pa4.z : 0.0f};
+    const float pb[3] = {okb ? pb4.x : 0.0f, okb ? pb4.y : 0.0f, okb ? pb4.z : 0.0f};
 #pragma unroll 1
-    for (uint32_t i = 0; i < kL / 4u; ++i) {
-        const uint32_t l = warp + 4u * i;
-        const LevelParams lp = lv[l];
-        uint32_t va = 0u, vb = 0u;
-        if (oka && okb) {
-            level_forward2(P, pa, lp, pb, lp, hash_mask, va, vb);
-        } else {
-            if (oka) va = level_forward(P, pa, lp, hash_mask);
-            if (okb) vb = level_forward(P, pb, lp, hash_mask);
-        }
-        *reinterpret_cast<uint32_t*>(feat + ra * kS32 + 2u * l) = va;
-        *reinterpret_cast<uint32_t*>(feat + rb * kS32 + 2u * l) = vb;
+    for (uint32_t i = 0; i < kL / 8u; ++i) {
+        const uint32_t l0 = warp + 8u * i, l1 = l0 + 4u;
+        const LevelParams lp0 = lv[l0], lp1 = lv[l1];
+        LevelGather g[4];
+        gather_level(P, pa, lp0, hash_mask, oka, g[0]);
+        gather_level(P, pb, lp0, hash_mask, okb, g[1]);
+        gather_level(P, pa, lp1, hash_mask, oka, g[2]);
+        gather_level(P, pb, lp1, hash_mask, okb, g[3]);
+        const uint32_t v0 = finish_level(g[0]), v1 = finish_level(g[1]), v2 = finish_level(g[2]), v3 = finish_level(g[3]);
+        *reinterpret_cast<uint32_t*>(feat + ra * kS32 + 2u * l0) = oka ? v0 : 0u;
+        *reinterpret_cast<uint32_t*>(feat + rb * kS32 + 2u * l0) = okb ? v1 : 0u;
+        *reinterpret_cast<uint32_t*>(feat + ra * kS32 + 2u * l1) = oka ? v2 : 0u;
+        *reinterpret_cast<uint32_t*>(feat + rb * kS32 + 2u * l1) = okb ? v3 : 0u;
     }
 }
 

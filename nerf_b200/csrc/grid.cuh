@@ -153,6 +153,49 @@ NB_DEV void level_forward2(const uint32_t* __restrict__ params, const float pa[3
     rb = interpolate(vb, wb);
 }
 
+// A (point, level) lookup split in two so that many lookups' loads can be in
+// flight at once: gather_level issues the four corner-pair loads and keeps
+// only what the interpolation needs (the loaded words, the cell fractions and
+// which aligned pairs came back swapped); finish_level interpolates exactly as
+// level_forward does (same weights, same fma order, one fp16 rounding).
+struct LevelGather {
+    uint2 v[4];      // corners (2k, 2k+1)
+    float f[3];
+    uint32_t swap;   // bit k: pair k was loaded as one aligned word pair in swapped order
+};
+NB_DEV void gather_level(const uint32_t* __restrict__ P, const float p[3], const LevelParams lp, uint32_t hash_mask,
+                         bool live, LevelGather& g) {
+    uint32_t i[3], idx[8];
+    level_cell(p, lp, i, g.f);
+    corner_entries(i, lp, hash_mask, idx);
+    g.swap = 0u;
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k) {
+        const uint32_t ea = idx[2 * k], eb = idx[2 * k + 1];
+        if (!live) {  // a dead row loads nothing
+            g.v[k] = make_uint2(0u, 0u);
+        } else if ((ea ^ eb) == 1u) {
+            g.v[k] = __ldg(reinterpret_cast<const uint2*>(P + (ea & ~1u)));
+            g.swap |= (ea & 1u) << k;
+        } else {
+            g.v[k].x = __ldg(P + ea);
+            g.v[k].y = __ldg(P + eb);
+        }
+    }
+}
+NB_DEV uint32_t finish_level(const LevelGather& g) {
+    float w[8];
+    corner_weights(g.f, w);
+    uint32_t v[8];
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k) {
+        const bool s = (g.swap >> k) & 1u;
+        v[2 * k] = s ? g.v[k].y : g.v[k].x;
+        v[2 * k + 1] = s ? g.v[k].x : g.v[k].y;
+    }
+    return interpolate(v, w);
+}
+
 // Scatter of one level's feature gradient (d0, d1) to the eight corner
 // entries with fp16x2 reductions performed at L2.
 NB_DEV void level_backward(uint32_t* grad, const float p[3], const LevelParams lp, uint32_t hash_mask, float d0, float d1) {
