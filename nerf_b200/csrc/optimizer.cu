@@ -109,7 +109,29 @@ __global__ void __launch_bounds__(256) k_grad_stats(const OptimArgs a) {
             stride = static_cast<uint64_t>(gridDim.x - kWgradBlocks) * blockDim.x;
         }
     }
-    for (uint64_t q = q0 + first; q < n_chunks; q += stride) {
+    // Hash-table part: four 16-byte loads in flight per thread before their
+    // sums (the loop is a chain of memory round trips otherwise); the same
+    // chunks in the same order as one at a time.
+    uint64_t q = q0 + first;
+    const uint64_t grid_end = n_chunks < grid_chunks ? n_chunks : grid_chunks;
+    for (; q + 3u * stride < grid_end; q += 4u * stride) {
+        uint4 u[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) u[j] = gg[q + j * stride];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t w[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 f = unpack_h2(w[k]);
+                if (!isfinite(f.x)) bad = 1u;
+                else sum = fmaf(f.x, f.x, sum);
+                if (!isfinite(f.y)) bad = 1u;
+                else sum = fmaf(f.y, f.y, sum);
+            }
+        }
+    }
+    for (; q < n_chunks; q += stride) {
         float v[8];
         if (q < grid_chunks) {
             const uint4 u = gg[q];
