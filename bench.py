@@ -187,6 +187,31 @@ def make_dataset(nb, views=None, renderer=None):
     return ds, time.time() - t0
 
 
+def cached_dataset(nb, args, rank, world):
+    """make_dataset, or with --scene-cache DIR the same views from DIR (rank 0 renders and writes them once; the
+    other ranks, and later runs of the same configuration, load them), so that a multi-GPU or multi-run measurement
+    of a large scene does not render it once per rank and per run.  The file holds exactly what the renderer
+    produced."""
+    if not args.scene_cache:
+        return make_dataset(nb, args.views)
+    import torch.distributed as dist
+    views = args.views or scene_cfg()["n_views"]
+    path = pathlib.Path(args.scene_cache) / f"scene_config{CONFIG}_views{views}.npz"
+    t0 = time.time()
+    if rank == 0 and not path.exists():
+        ds, _ = make_dataset(nb, args.views)
+        path.parent.mkdir(parents=True, exist_ok=True)
+        tmp = path.with_suffix(".tmp.npz")
+        np.savez(tmp, images=ds.images, cameras=ds.cameras, intrinsics=np.array(ds.intrinsics, np.float64))
+        tmp.rename(path)
+    if world > 1:
+        dist.barrier()
+    z = np.load(path)
+    ds = nb.Dataset(np.ascontiguousarray(z["images"]), np.ascontiguousarray(z["cameras"]),
+                    tuple(float(x) for x in z["intrinsics"]))
+    return ds, time.time() - t0
+
+
 def oracle_scene(**cfg):
     """nb.make_scene through the oracle library (oracle_scene_render: the same scene.cpp, built into liboracle.so)."""
     import nerf_b200 as nb  # the Dataset container only; this loads no native library
@@ -213,7 +238,7 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local), timeout=__import__("datetime").timedelta(seconds=300))
 
     lib = abi.load()
-    ds, gen_s = make_dataset(nb, args.views)
+    ds, gen_s = cached_dataset(nb, args, rank, world)
 
     ctx = nb.Context(ds, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
                      options=options(nb))
@@ -232,8 +257,14 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()  # running well before the timed region
-    for _ in range(args.pretrain):
-        step()
+    state_in = args.state_in and pathlib.Path(args.state_in).exists() and world == 1
+    if state_in:  # the pretrained training state of an earlier run (exact resume), instead of the pretrain steps
+        ctx.load_state(args.state_in)
+    else:
+        for _ in range(args.pretrain):
+            step()
+        if args.state_out and world == 1:
+            ctx.save_state(args.state_out)
     for _ in range(args.warmup):
         step()
     c0 = ctx.counters()
@@ -922,6 +953,13 @@ def main():
     ap.add_argument("--psnr-views", type=int, default=20)
     ap.add_argument("--e2e-steps", type=int, default=1000)
     ap.add_argument("--views", type=int, default=None)
+    ap.add_argument("--state-out", default=None,
+                    help="one GPU: save the training state after the pretrain steps (for --state-in)")
+    ap.add_argument("--state-in", default=None,
+                    help="one GPU: start from this saved training state instead of running the pretrain steps "
+                         "(profilers: a few launches before the captured ones); ignored when the file is absent")
+    ap.add_argument("--scene-cache", default=None,
+                    help="directory for the rendered training views (rendered once by rank 0, then loaded)")
     ap.add_argument("--skip-render", action="store_true")
     ap.add_argument("--skip-e2e", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
