@@ -361,13 +361,14 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-# Per training sample, from one ncu capture of this build's step kernels on config 2: L2 sectors the forward's
-# gathers request from L2 (hash-table lookups after coalescing and pairing), and L2 reduction operations the
-# scatter issues (after run merging and .v4 pairing).
-NCU_PER_SAMPLE = {"field_forward_l2_read_sectors": None, "grid_scatter_l2_red_ops": 48.06}
+# Per training sample, from one ncu capture of this build's step kernels on config 2 (steady state, the eager
+# step resumed from a saved training state): L1 sectors the forward's gathers request (the hash-table lookups after
+# coalescing and pairing; about half hit in L1), and L2 f16x2 reduction operations the scatter issues (after run
+# merging and 16-byte pairing).  Counts over the captured launch / the samples of that step.
+NCU_PER_SAMPLE = {"field_forward_l1_sectors": 48.1, "field_forward_l2_sectors": 26.6, "grid_scatter_l2_red_ops": 38.0}
 # DRAM bytes (read + write) per launch from the same capture (cold-cache replay, so the hash table and its gradient
 # count as DRAM traffic although a live step keeps them in L2).
-NCU_TRAFFIC = {"mlp_backward": 36.59e6, "grid_scatter": 73.13e6, "field_forward": 31.67e6, "adam": 311.31e6}
+NCU_TRAFFIC = {"mlp_backward": 36.41e6, "grid_scatter": 71.09e6, "field_forward": 30.58e6, "adam": 311.31e6}
 
 
 def measured_peaks():
@@ -396,9 +397,10 @@ def kernel_table(ctx, prof_ms, samples, l2, world):
         "sample_bits": ("latency", samples * 4),
         # kept t read, pos/dt 16 + ray id 4 written
         "sample_write": ("hbm", samples * (4 + 16 + 4)),
-        # 128 corner lookups of 4 B per sample (16 levels x 8 corners), against the hashed 4-byte gather probe;
-        # bytes: pos/dt 16 + ray id 4 + 512 corner bytes + 112 training row + 16 raw out
-        "field_forward": ("l2_gather", samples * 128),
+        # L1 sectors the corner lookups request per sample (ncu), against the sector rate of the hashed 4-byte
+        # gather probe (one sector per load); algorithmic bytes: pos/dt 16 + ray id 4 + 512 corner bytes + 112
+        # training row + 16 raw out, against the 16-byte L2 read probe
+        "field_forward": ("l2_gather", samples * NCU_PER_SAMPLE["field_forward_l1_sectors"]),
         # raw 16 + pos/dt 16 read twice, dout 16 written, transmittance 8
         "composite": ("hbm", samples * (2 * 32 + 16 + 8)),
         # forward recompute 20,480 + input-gradient 20,480 + weight-gradient 20,480 FLOP per sample
@@ -428,11 +430,10 @@ def kernel_table(ctx, prof_ms, samples, l2, world):
             elif bound == "tensor":
                 rec.update(achieved=amount / t / 1e12, peak=pk["bf16_tflops_sustained"], unit="TFLOP/s")
             elif bound == "l2_gather":
-                rec.update(achieved=amount / t / 1e9, peak=l2["gather_4b_gops"], unit="G lookups/s",
+                rec.update(achieved=amount / t / 1e9, peak=l2["gather_4b_gops"], unit="G L1 sectors/s",
+                           corner_lookups_g_per_s=samples * 128 / t / 1e9,
+                           l2_sectors_g_per_s=samples * NCU_PER_SAMPLE["field_forward_l2_sectors"] / t / 1e9,
                            l2_read_gbs=samples * 660 / t / 1e9, l2_read_frac=samples * 660 / t / 1e9 / l2["read_gbs"])
-                sec = NCU_PER_SAMPLE["field_forward_l2_read_sectors"]
-                if sec:
-                    rec["l2_sectors_g_per_s"] = samples * sec / t / 1e9
             elif bound == "l2_red":
                 rec.update(achieved=amount / t / 1e9, peak=l2["red_v4_f16x2_gops"], unit="G red ops/s",
                            corner_updates_g_per_s=samples * 128 / t / 1e9)
@@ -520,7 +521,7 @@ def roofline(kernels):
     dom = max(timed, key=lambda k: k["ms"])
     src = {"hbm": f"MEASURED_PEAKS.json hbm_gbs ({pk['source']})",
            "tensor": f"MEASURED_PEAKS.json bf16_tflops_sustained ({pk['source']})",
-           "l2_gather": "live probe: 4-byte loads at hashed addresses of an L2-resident 32 MB buffer",
+           "l2_gather": "live probe: 4-byte loads at hashed addresses of an L2-resident 32 MB buffer (one sector each)",
            "l2_red": "live probe: 16-byte f16x2 reductions at hashed addresses of an L2-resident 32 MB buffer",
            "nvlink": "measured peer copy, 770 GB/s per direction"}[dom["bound"]]
     return {"kernel": dom["kernel"], "bound": dom["bound"], "achieved": dom["achieved"], "peak": dom["peak"],

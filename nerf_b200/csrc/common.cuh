@@ -104,14 +104,6 @@ NB_DEV void load_b_nk(uint32_t b[4], const __half* base, uint32_t stride, uint32
     const uint32_t k = k0 + (mi & 1u) * 8u;
     ldsm_x4(b, base + n * stride + k);
 }
-// B fragment of one n-tile (n0) for B[k][n] = W[n][k], W stored [n][k].
-NB_DEV void load_b_nk1(uint32_t b[2], const __half* base, uint32_t stride, uint32_t n0, uint32_t k0, uint32_t lane) {
-    const uint32_t n = n0 + (lane & 7u);
-    const uint32_t k = k0 + ((lane >> 3) & 1u) * 8u;
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n"
-                 : "=r"(b[0]), "=r"(b[1])
-                 : "r"(smem_u32(base + n * stride + k)));
-}
 // B fragments of two n-tiles for B stored [k][n] (n contiguous).
 NB_DEV void load_b_kn(uint32_t b[4], const __half* base, uint32_t stride, uint32_t n0, uint32_t k0, uint32_t lane) {
     const uint32_t mi = lane >> 3;

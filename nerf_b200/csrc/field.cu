@@ -43,10 +43,6 @@ constexpr uint32_t kWC0 = kWD1 + 16 * kS64;   // 64 x 32
 constexpr uint32_t kWC1 = kWC0 + 64 * kS32;   // 64 x 64
 constexpr uint32_t kWC2 = kWC1 + 64 * kS64;   // 16 x 64
 constexpr uint32_t kWTotal = kWC2 + 16 * kS64;
-// The forward kernels evaluate only the first 8 rows of the colour output
-// layer (3 are used), so their copy stops there: 1,152 bytes less shared
-// memory per CTA, which with the 16-level table lets 6 CTAs share an SM.
-constexpr uint32_t kWTotalFwd = kWC2 + 8 * kS64;
 
 
 __device__ __forceinline__ void copy_matrix(__half* dst, uint32_t stride, const __half* src, uint32_t rows, uint32_t cols) {
@@ -57,13 +53,13 @@ __device__ __forceinline__ void copy_matrix(__half* dst, uint32_t stride, const 
     }
 }
 
-__device__ __forceinline__ void load_weights(__half* w, const __half* mlp, bool density_only, uint32_t colour_rows = 16) {
+__device__ __forceinline__ void load_weights(__half* w, const __half* mlp, bool density_only) {
     copy_matrix(w + kWD0, kS32, mlp + kMlpD0, 64, 32);
     copy_matrix(w + kWD1, kS64, mlp + kMlpD1, 16, 64);
     if (density_only) return;
     copy_matrix(w + kWC0, kS32, mlp + kMlpC0, 64, 32);
     copy_matrix(w + kWC1, kS64, mlp + kMlpC1, 64, 64);
-    copy_matrix(w + kWC2, kS64, mlp + kMlpC2, colour_rows, 64);
+    copy_matrix(w + kWC2, kS64, mlp + kMlpC2, 16, 64);
 }
 
 // Real SH bands 0..3 of a unit direction; evaluation order and rounding
@@ -104,17 +100,6 @@ __device__ __forceinline__ void gemm_nk(float acc[NT][4], const uint32_t a[KC][4
             mma16816(acc[2 * np], a[kc], b[0], b[1]);
             mma16816(acc[2 * np + 1], a[kc], b[2], b[3]);
         }
-    }
-}
-// One n-tile (outputs n0..n0+7) of A[KC] x W^T, W stored [n][k].
-template <int KC>
-__device__ __forceinline__ void gemm_nk1(float acc[4], const uint32_t a[KC][4], const __half* W, uint32_t stride, uint32_t lane) {
-    acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
-#pragma unroll
-    for (int kc = 0; kc < KC; ++kc) {
-        uint32_t b[2];
-        load_b_nk1(b, W, stride, 0u, kc * 16u, lane);
-        mma16816(acc, a[kc], b[0], b[1]);
     }
 }
 // out[NT] = A[KC] x W with W stored [k][n] (the transpose product of the backward pass).
@@ -177,14 +162,14 @@ struct Smem {
     float4* pos;
     LevelParams* lv;
 };
-constexpr size_t kFwdBase = (kWTotalFwd + 2 * kRows * kS32) * 2 + kRows * 16 + kL * 16;
+constexpr size_t kFwdBase = (kWTotal + 2 * kRows * kS32) * 2 + kRows * 16 + kMaxLevels * 16;
 constexpr size_t kFwdStage = kRows * 16 + kRows * 4;
 constexpr size_t kFwdSmem = kFwdBase + 2 * kFwdStage;
 
 __device__ __forceinline__ Smem carve(unsigned char* raw) {
     Smem s{};
     s.w = reinterpret_cast<__half*>(raw);
-    s.feat = s.w + kWTotalFwd;
+    s.feat = s.w + kWTotal;
     s.xc = s.feat + kRows * kS32;
     s.pos = reinterpret_cast<float4*>(s.xc + kRows * kS32);
     s.lv = reinterpret_cast<LevelParams*>(s.pos + kRows);
@@ -430,7 +415,7 @@ __device__ __forceinline__ void forward_colour(const __half* w, const __half* xc
     relu_to_a<8>(acc, c.h1);
     gemm_nk<8, 4>(acc, c.h1, w + kWC1, kS64, lane);
     relu_to_a<8>(acc, c.h2);
-    gemm_nk1<4>(c.yc[0], c.h2, w + kWC2, kS64, lane);  // colour outputs 0..7 (0..2 are used)
+    gemm_nk<2, 4>(c.yc, c.h2, w + kWC2, kS64, lane);
 }
 
 __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, const int mode) {
@@ -439,7 +424,7 @@ __global__ void __launch_bounds__(kThreads) k_field_forward(const FieldArgs a, c
     const uint32_t n = row_count(a, mode);
     if (n == 0u) return;
     const __half* mlp = static_cast<const __half*>(a.params16) + a.mlp_offset;
-    load_weights(s.w, mlp, mode == kFieldOccupancy, 8u);
+    load_weights(s.w, mlp, mode == kFieldOccupancy);
     load_levels(a.lt, s.lv);
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t g = lane >> 2, t = lane & 3u;
@@ -885,7 +870,7 @@ __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
     float4* raw_s = reinterpret_cast<float4*>(slots + kRows);
     float* dt_s = reinterpret_cast<float*>(raw_s + kRows);
     const __half* mlp = static_cast<const __half*>(a.params16) + a.mlp_offset;
-    load_weights(s.w, mlp, false, 8u);
+    load_weights(s.w, mlp, false);
     if (threadIdx.x < a.lt.n_levels) {
         const uint32_t l = threadIdx.x;
         s.lv[l] = LevelParams{a.lt.scale[l], a.lt.res[l], a.lt.dense[l], a.lt.offset[l]};
