@@ -200,12 +200,17 @@ def cached_dataset(nb, args, rank, world):
     t0 = time.time()
     if rank == 0 and not path.exists():
         ds, _ = make_dataset(nb, args.views)
-        path.parent.mkdir(parents=True, exist_ok=True)
-        tmp = path.with_suffix(".tmp.npz")
-        np.savez(tmp, images=ds.images, cameras=ds.cameras, intrinsics=np.array(ds.intrinsics, np.float64))
-        tmp.rename(path)
+        try:
+            path.parent.mkdir(parents=True, exist_ok=True)
+            tmp = path.with_suffix(".tmp.npz")
+            np.savez(tmp, images=ds.images, cameras=ds.cameras, intrinsics=np.array(ds.intrinsics, np.float64))
+            tmp.rename(path)
+        except OSError as e:  # no room for the cache: every rank renders its own copy
+            print(f"scene cache not written ({e})", file=sys.stderr)
     if world > 1:
         dist.barrier()
+    if not path.exists():
+        return make_dataset(nb, args.views)
     z = np.load(path)
     ds = nb.Dataset(np.ascontiguousarray(z["images"]), np.ascontiguousarray(z["cameras"]),
                     tuple(float(x) for x in z["intrinsics"]))
