@@ -509,7 +509,9 @@ NerfStatus Context::configure(const NerfTrainingConfig& c) {
     const bool bounded = opt.target_samples_per_step != 0u || opt.max_samples_per_step != 0u;
     uint64_t cap;
     if (bounded) {
-        cap = opt.max_samples_per_step ? opt.max_samples_per_step : 2ull * opt.target_samples_per_step;
+        // The documented rule (NerfB200Options::max_samples_per_step): an
+        // explicit cap, else rays x steps, within the sample buffers.
+        cap = opt.max_samples_per_step ? opt.max_samples_per_step : total;
         cap = std::min<uint64_t>(cap, max_sample_steps);
     } else {
         if (total > max_sample_steps || total > 0xFFFFFFFFull) return NERF_STATUS_INVALID_USAGE;
