@@ -35,7 +35,6 @@ __device__ __forceinline__ float sigmoidf(float x) { return __fdiv_rn(1.0f, __fa
 
 __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a) {
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t k = blockIdx.x * kWarps + warp;
     // Data parallel: this rank's sample count rides with the loss in the
     // exchanged MLP-gradient buffer, so every rank sizes its next batch from
     // the same global count (exact in fp32 below 2^24).
@@ -50,8 +49,12 @@ __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a
         n = a.state->n_active;
         inv_norm = n == 0u ? 0.0f : __fdiv_rn(1.0f, __fmul_rn(static_cast<float>(n), static_cast<float>(a.dp_world)));
     }
-    float loss = 0.0f;
-    if (k < n) {
+    // Warp per ray, grid-stride over the rays: the grid is sized to the SMs
+    // (one wave), not to the ray capacity, so the capacity's thousands of idle
+    // blocks are never scheduled.
+    float loss_sum = 0.0f;
+    for (uint32_t k = blockIdx.x * kWarps + warp; k < n; k += gridDim.x * kWarps) {
+        float loss = 0.0f;
         const RayRecord ray = a.rays[k];
         const uint32_t b = ray.begin, count = ray.count;
         const float stop = a.stop_transmittance;
@@ -186,10 +189,11 @@ __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a
             if (a.ray_loss) a.ray_loss[k] = loss;
             if (a.ray_used) a.ray_used[k] = used;
         }
+        loss_sum += loss;
     }
-    // Block sum of the ray losses (lane 0 of each warp holds its ray's), normalised, added to the loss slot.
+    // Block sum of the ray losses (lane 0 of each warp holds its rays'), normalised, added to the loss slot.
     __shared__ float part[kWarps];
-    if (lane == 0u) part[warp] = loss;
+    if (lane == 0u) part[warp] = loss_sum;
     __syncthreads();
     if (threadIdx.x == 0u) {
         float bs = 0.0f;
@@ -203,7 +207,15 @@ __global__ void __launch_bounds__(kWarps * 32) k_composite(const CompositeArgs a
 cudaError_t launch_composite(const CompositeArgs& a, cudaStream_t s) {
     const uint32_t rays = a.direct ? a.n_rays : a.max_rays;
     if (rays == 0u) return cudaSuccess;
-    k_composite<<<(rays + kWarps - 1u) / kWarps, kWarps * 32u, 0, s>>>(a);
+    static int sms = 0;
+    if (sms == 0) {
+        int dev = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return e;
+    }
+    const uint32_t want = (rays + kWarps - 1u) / kWarps, cap = 8u * static_cast<uint32_t>(sms);
+    k_composite<<<want < cap ? want : cap, kWarps * 32u, 0, s>>>(a);
     return cudaGetLastError();
 }
 

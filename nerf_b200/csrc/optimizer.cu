@@ -39,14 +39,17 @@ __device__ __forceinline__ float wgrad_block_sum(const float* __restrict__ parti
     const float* p = partials + block * kWgradParamsPerBlock + lane;
     float s = 0.0f;
     uint32_t c = c0;
-    for (; c + 32u <= c1; c += 32u) {
+    // Rows in batches of 32 with every load in flight before the adds; the
+    // last, partial batch the same way (rows past c1 add an exact zero), so a
+    // warp takes one memory round trip per batch.
+    for (; c < c1; c += 32u) {
         float v[32];
 #pragma unroll
-        for (uint32_t k = 0; k < 32u; ++k) v[k] = __ldcs(p + static_cast<unsigned long long>(c + k) * kMlpParams);
+        for (uint32_t k = 0; k < 32u; ++k)
+            v[k] = c + k < c1 ? __ldcs(p + static_cast<unsigned long long>(c + k) * kMlpParams) : 0.0f;
 #pragma unroll
         for (uint32_t k = 0; k < 32u; ++k) s += v[k];
     }
-    for (; c < c1; ++c) s += __ldcs(p + static_cast<unsigned long long>(c) * kMlpParams);
     ws[warp][lane] = s;
     __syncthreads();
     float g = 0.0f;
