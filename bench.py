@@ -18,8 +18,11 @@ events on each context's stream, max over ranks).  e2e: the same metric for
 a whole job through the C ABI from pinned host memory: create (uploads the
 images), configure, then every step nerf_train_step + nerf_read_train_stats
 (20-byte device-to-host read).  Extra keys: roofline of the dominant kernel
-from event-timed kernel-by-kernel steps, per-kernel times, render MRays/s
-(config 3), cpu_baseline (the CPU oracle on a bounded sample).
+from event-timed kernel-by-kernel steps, per-kernel times with their own
+bounds, held-out PSNR after the configuration's step count (training goes on
+after the timed steps: config 2 20k steps, config 4 10k), render MRays/s
+(config 3: the 200 orbit views), cpu_baseline (the CPU oracle on a bounded
+sample of the same step shape).
 
 --impl reference times the reference algorithm's CPU implementation (the
 oracle port; the reference backend has no CPU path) on the host cores, rank 0
@@ -319,7 +322,13 @@ def run_ours(args):
     l2 = l2_peaks(stream)
     kernels = kernel_table(ctx, prof, mean_samples, l2, world)
 
-    psnr = psnr_heldout(nb, ctx, args) if rank == 0 else None
+    # Train on to the configuration's step count (config 2: 20k steps, config 4: 10k) before the held-out PSNR;
+    # every rank steps (the data-parallel step is collective), rank 0 measures.
+    psnr = None
+    if args.psnr_views > 0:
+        while ctx.counters().frame_index < args.psnr_steps:
+            ctx.train_step()
+        psnr = psnr_heldout(nb, ctx, args) if rank == 0 else None
     render = None
     if not args.skip_render:
         render = run_render(nb, ctx, rank, world, args)
@@ -560,7 +569,7 @@ def psnr_heldout(nb, ctx, args):
         errs.append(float(np.mean((out - ref) ** 2)))
     psnr = [10.0 * np.log10(1.0 / max(e, 1e-12)) for e in errs]
     return {"value": float(np.mean(psnr)), "unit": "dB", "views": n, "resolution": f"{W}x{H}",
-            "train_steps": args.pretrain + 2 * args.warmup + args.steps,
+            "train_steps": int(ctx.counters().frame_index),
             "note": "mean over held-out views (config 2: the cameras after the training views; config 4: ring "
                     "positions between the training views) of PSNR against the exact render composited on white; "
                     "rendered with the training occupancy grid, T < 1e-4 termination"}
@@ -935,7 +944,7 @@ def reference_cuda(args):
         return {"unavailable": "oracle/_ref/libref_stock.so is not built (the reference checkout was absent at build)"}
     cmd = [sys.executable, "-m", "oracle.ref_backend", "--pretrain", str(args.pretrain), "--steps",
            str(args.reference_cuda_steps), "--render-views", "4", "--psnr-views", "5", "--psnr-steps",
-           str(args.pretrain + 2 * args.warmup + args.steps)]  # the steps after which the own arm measures PSNR
+           str(args.psnr_steps)]  # the steps after which the own arm measures PSNR
     try:
         r = subprocess.run(cmd, cwd=str(ROOT), capture_output=True, text=True, timeout=900)
     except subprocess.TimeoutExpired:
@@ -955,8 +964,10 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--pretrain", type=int, default=2000)
     ap.add_argument("--profile-steps", type=int, default=20)
-    ap.add_argument("--render-views", type=int, default=20)
+    ap.add_argument("--render-views", type=int, default=200, help="config-3 views rendered (the configuration's 200)")
     ap.add_argument("--psnr-views", type=int, default=20)
+    ap.add_argument("--psnr-steps", type=int, default=None,
+                    help="training steps before the held-out PSNR (default: the configuration's, 20k / 10k)")
     ap.add_argument("--e2e-steps", type=int, default=1000)
     ap.add_argument("--views", type=int, default=None)
     ap.add_argument("--state-out", default=None,
@@ -998,6 +1009,8 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "config 4 needs occupancy cascades and an AABB of "
                               "scale 16, which the reference backend does not have (one [0,1]^3 grid)"}), flush=True)
             return
+    if args.psnr_steps is None:
+        args.psnr_steps = 10000 if CONFIG == 4 else 20000
     if args.micro:
         run_micro(args)
     elif args.impl == "reference":
