@@ -247,6 +247,10 @@ def run_ours(args):
 
     lib = abi.load()
     ds, gen_s = cached_dataset(nb, args, rank, world)
+    ds_pinned = None
+    if not args.skip_e2e:  # host buffer of the e2e job, pinned up front (as a caller would keep its images)
+        pinned_imgs = torch.from_numpy(ds.images).pin_memory()
+        ds_pinned = nb.Dataset(pinned_imgs.numpy(), ds.cameras, ds.intrinsics)
 
     ctx = nb.Context(ds, grid_res=GRID_RES, max_sample_steps=2 * TARGET_SAMPLES, max_batch_rays=1 << 16,
                      options=options(nb))
@@ -337,8 +341,6 @@ def run_ours(args):
     if not args.skip_e2e:
         ctx.close()
         torch.cuda.synchronize()
-        pinned_imgs = torch.from_numpy(ds.images).pin_memory()  # host buffer of the e2e job
-        ds_pinned = nb.Dataset(pinned_imgs.numpy(), ds.cameras, ds.intrinsics)
         e2e = run_e2e(nb, lib, ds_pinned, rank, world, args)
 
     cpu = None
