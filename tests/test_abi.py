@@ -158,3 +158,18 @@ def test_extension_struct_mirrors_match_c_layout(tmp_path):
         for fname, _ in c._fields_:
             assert getattr(c, fname).offset == int(got[f"{n}.{fname}"]), (n, fname)
     assert int(got["NERF_B200_STEP_KERNELS"]) == len(abi.STEP_KERNELS)
+
+
+def test_oracle_scene_renderer_matches_the_library():
+    """The oracle library carries the same scene renderer (oracle_scene_render, compiled from the package's
+    scene.cpp) so that the benchmark's reference arm can build its datasets without loading libnerf_b200.so: its
+    images, cameras and intrinsics equal the library's bit for bit."""
+    from oracle import oracle
+    for kw in (dict(kind=0, seed=0, n_views=3, width=40, height=32),
+               dict(kind=1, seed=2, n_primitives=12, density=100.0, extent=1.0, size_min=0.1, size_max=0.6, n_views=2,
+                    width=48, height=48, radius=4.0, camera_mode=1),
+               dict(kind=2, seed=4, n_primitives=10, density=100.0, extent=6.0, size_min=0.1, size_max=0.6, n_views=2,
+                    width=40, height=24, fov=1.2, radius=3.0, camera_mode=3, orbit_elevation=0.3, orbit_views=6)):
+        a = nerf_b200.make_scene(n_threads=2, **kw)
+        imgs, cams, intr = oracle.make_scene(n_threads=3, **kw)
+        assert np.array_equal(a.images, imgs) and np.array_equal(a.cameras, cams) and a.intrinsics == intr
