@@ -274,7 +274,10 @@ NERF_API NerfStatus nerf_b200_png_write(const char* path, const uint8_t* rgba8, 
 
 /* ------------------------------------- kernel-level entry points (tests) */
 /* All pointers are device pointers; stream is a cudaStream_t (NULL = legacy
- * default stream).  Calls are asynchronous. */
+ * default stream).  Calls are asynchronous.  Parameter and gradient tables
+ * (params_f16, grad_f16, grid_grad_f16, mlp_params_f16) start on a 16-byte
+ * boundary: they are read and reduced in 16-byte blocks, and a misaligned
+ * table is refused with NERF_STATUS_INVALID_USAGE. */
 NERF_API NerfStatus nerf_b200_grid_forward(const NerfB200GridLayout* layout, const float* pos_unit, uint32_t n,
                                            const void* params_f16, void* feat_f16, void* stream);
 NERF_API NerfStatus nerf_b200_grid_backward(const NerfB200GridLayout* layout, const float* pos_unit, uint32_t n,

@@ -705,7 +705,7 @@ cudaError_t Context::enqueue_step(cudaStream_t s, cudaEvent_t* ev) {
     op.n_partials = n_partials;
     op.n_grid = n_grid;
     op.n_params = n_params;
-    op.stats_blocks = grad_stats_blocks(n_params);
+    op.stats_blocks = grad_stats_blocks(n_params, !dp_active());
     op.mlp_in = mlp_grad;
     op.world = dp_world;
     if (dp_peer) {
@@ -1750,9 +1750,14 @@ NERF_API NerfStatus nerf_b200_train_step_profiled(void* context, NerfB200StepPro
 }
 
 // ------------------------------------------------------ kernel-level entries
+// Parameter and gradient tables of the kernel-level entry points are read
+// and reduced in 16-byte blocks.
+static bool misaligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) != 0u; }
+
 NERF_API NerfStatus nerf_b200_grid_forward(const NerfB200GridLayout* layout, const float* pos, uint32_t n, const void* params,
                                            void* feat, void* stream) {
     if (!layout || (n && (!pos || !params || !feat))) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(params)) return NERF_STATUS_INVALID_USAGE;
     const nb::LevelTable lt = nb::make_level_table(*reinterpret_cast<const nb::GridLayout*>(layout));
     return nb::cuda_status(nb::launch_grid_forward(lt, pos, n, params, feat, static_cast<cudaStream_t>(stream)));
 }
@@ -1760,6 +1765,7 @@ NERF_API NerfStatus nerf_b200_grid_forward(const NerfB200GridLayout* layout, con
 NERF_API NerfStatus nerf_b200_grid_backward(const NerfB200GridLayout* layout, const float* pos, uint32_t n, const void* dfeat,
                                             void* grad, void* stream) {
     if (!layout || (n && (!pos || !dfeat || !grad))) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(grad)) return NERF_STATUS_INVALID_USAGE;
     const nb::LevelTable lt = nb::make_level_table(*reinterpret_cast<const nb::GridLayout*>(layout));
     return nb::cuda_status(nb::launch_grid_backward(lt, pos, n, dfeat, grad, static_cast<cudaStream_t>(stream)));
 }
@@ -1767,6 +1773,7 @@ NERF_API NerfStatus nerf_b200_grid_backward(const NerfB200GridLayout* layout, co
 NERF_API NerfStatus nerf_b200_field_forward(const NerfB200GridLayout* layout, const void* params, const float* pos,
                                             const float* dirs, uint32_t n, void* feat, float* raw, void* stream) {
     if (!layout || layout->n_levels != 16u || (n && (!params || !pos || !dirs || !raw))) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(params)) return NERF_STATUS_INVALID_USAGE;
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     nb::FieldArgs a{};
     a.lt = nb::make_level_table(*reinterpret_cast<const nb::GridLayout*>(layout));
@@ -1790,6 +1797,7 @@ NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, c
                                              const float* dirs, uint32_t n, const void* feat, const float* dout,
                                              void* grid_grad, float* partials, float* mlp_grad, void* stream) {
     if (!layout || layout->n_levels != 16u || !params || !partials || !mlp_grad || !grid_grad) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(params) || misaligned16(grid_grad)) return NERF_STATUS_INVALID_USAGE;
     if (n && (!pos || !dirs || !feat || !dout)) return NERF_STATUS_INVALID_USAGE;
     if (n > 0x7FFFFFFFu) return NERF_STATUS_INVALID_USAGE;  // rows are indexed with 32-bit tile counters
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
@@ -1818,6 +1826,7 @@ NERF_API NerfStatus nerf_b200_field_backward(const NerfB200GridLayout* layout, c
 NERF_API NerfStatus nerf_b200_mlp_forward(const void* mlp_params, const void* feat, const float* dirs, uint32_t n, float* raw,
                                           void* stream) {
     if (n && (!mlp_params || !feat || !dirs || !raw)) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(mlp_params)) return NERF_STATUS_INVALID_USAGE;
     if (n == 0u) return NERF_STATUS_OK;
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     nb::FieldArgs a{};
@@ -1833,6 +1842,7 @@ NERF_API NerfStatus nerf_b200_mlp_forward(const void* mlp_params, const void* fe
 NERF_API NerfStatus nerf_b200_mlp_forward_tc(const void* mlp_params, const void* feat, const float* dirs, uint32_t n, float* raw,
                                              uint32_t* error_word, void* stream) {
     if (n && (!mlp_params || !feat || !dirs || !raw || !error_word)) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(mlp_params)) return NERF_STATUS_INVALID_USAGE;
     if (n == 0u) return NERF_STATUS_OK;
     return nb::cuda_status(nb::launch_mlp_forward_tc(mlp_params, feat, dirs, n, raw, error_word, static_cast<cudaStream_t>(stream)));
 }
@@ -1847,6 +1857,7 @@ NERF_API NerfStatus nerf_b200_mlp_backward_tc(const void* mlp_params, const void
                                               const float* dout, void* dfeat, float* partials, float* mlp_grad, uint32_t* error_word,
                                               void* stream) {
     if (!mlp_params || !partials || !mlp_grad || !error_word) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(mlp_params)) return NERF_STATUS_INVALID_USAGE;
     if (n && (!feat || !dirs || !dout || !dfeat)) return NERF_STATUS_INVALID_USAGE;
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -1866,6 +1877,7 @@ NERF_API NerfStatus nerf_b200_mlp_backward_tc(const void* mlp_params, const void
 NERF_API NerfStatus nerf_b200_mlp_backward(const void* mlp_params, const void* feat, const float* dirs, uint32_t n,
                                            const float* dout, void* dfeat, float* partials, float* mlp_grad, void* stream) {
     if (!mlp_params || !partials || !mlp_grad) return NERF_STATUS_INVALID_USAGE;
+    if (misaligned16(mlp_params)) return NERF_STATUS_INVALID_USAGE;
     if (n && (!feat || !dirs || !dout || !dfeat)) return NERF_STATUS_INVALID_USAGE;
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     const cudaStream_t s = static_cast<cudaStream_t>(stream);

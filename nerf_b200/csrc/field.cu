@@ -336,7 +336,7 @@ __device__ __forceinline__ void load_rows(const FieldArgs& a, int mode, const Sm
 // (row, level) lookups -- 16 to 32 loads -- in flight before it waits.
 // ok(row, pos) says whether a row is live; a dead row loads nothing and
 // stores zeros.
-template <class Ok>
+template <class Gather = LevelGather, class Ok>
 __device__ __forceinline__ void encode_rows(const uint32_t* __restrict__ P, const LevelParams* lv, uint32_t hash_mask,
                                             const float4* pos, __half* feat, Ok ok) {
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
@@ -349,7 +349,7 @@ __device__ __forceinline__ void encode_rows(const uint32_t* __restrict__ P, cons
     for (uint32_t i = 0; i < kL / 8u; ++i) {
         const uint32_t l0 = warp + 8u * i, l1 = l0 + 4u;
         const LevelParams lp0 = lv[l0], lp1 = lv[l1];
-        LevelGather g[4];
+        Gather g[4];
         gather_level(P, pa, lp0, hash_mask, oka, g[0]);
         gather_level(P, pb, lp0, hash_mask, okb, g[1]);
         gather_level(P, pa, lp1, hash_mask, oka, g[2]);
@@ -985,8 +985,8 @@ __global__ void __launch_bounds__(kThreads) k_render(const RenderArgs a) {
             if (!has_row) s.pos[tid] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         }
         if (!__syncthreads_or(has_row)) break;
-        // Encode the tile's live rows.
-        encode_rows(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
+        // Encode the tile's live rows (16-byte corner-pair loads: fewer sectors per pixel).
+        encode_rows<LevelGatherWide>(static_cast<const uint32_t*>(a.params16), s.lv, a.lt.hash_mask, s.pos, s.feat,
                     [](uint32_t, const float4& p) { return p.w > 0.0f; });
         __syncthreads();
         {

@@ -196,6 +196,56 @@ NB_DEV uint32_t finish_level(const LevelGather& g) {
     return interpolate(v, w);
 }
 
+struct LevelGatherWide {
+    uint4 q[4];    // pair k: the aligned 16-byte block holding corners 2k and 2k+1, or those two corners in .x, .y
+    float f[3];
+    uint32_t sel;  // pair k: bits 4k..4k+1 = word of corner 2k in q[k], bits 4k+2..4k+3 = word of corner 2k+1
+};
+// The same lookup with 16-byte loads.  The x-neighbours of a pair share their
+// aligned 16-byte block whenever their entries differ in the two low bits
+// only: always for x even (entries e and e ^ 1 on hashed levels, e and e + 1
+// on dense ones) and for half of the odd x; then the pair is one 16-byte load,
+// which touches one sector where two 4-byte loads would touch it twice.  It
+// holds twice the registers per lookup: the renderer gains from it (fewer
+// sectors per pixel), the training forward, whose warps share more sectors
+// and need more lookups in flight, does not.  The table must start on a
+// 16-byte boundary.
+NB_DEV void gather_level(const uint32_t* __restrict__ P, const float p[3], const LevelParams lp, uint32_t hash_mask,
+                         bool live, LevelGatherWide& g) {
+    uint32_t i[3], idx[8];
+    level_cell(p, lp, i, g.f);
+    corner_entries(i, lp, hash_mask, idx);
+    g.sel = 0u;
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k) {
+        const uint32_t ea = idx[2 * k], eb = idx[2 * k + 1];
+        if (!live) {  // a dead row loads nothing
+            g.q[k] = make_uint4(0u, 0u, 0u, 0u);
+            g.sel |= 4u << (4u * k);
+        } else if (((ea ^ eb) >> 2) == 0u) {
+            g.q[k] = __ldg(reinterpret_cast<const uint4*>(P + (ea & ~3u)));
+            g.sel |= ((ea & 3u) | ((eb & 3u) << 2)) << (4u * k);
+        } else {
+            g.q[k] = make_uint4(__ldg(P + ea), __ldg(P + eb), 0u, 0u);
+            g.sel |= 4u << (4u * k);
+        }
+    }
+}
+NB_DEV uint32_t pick_word(const uint4 q, uint32_t w) {
+    return (w & 2u) ? ((w & 1u) ? q.w : q.z) : ((w & 1u) ? q.y : q.x);
+}
+NB_DEV uint32_t finish_level(const LevelGatherWide& g) {
+    float w[8];
+    corner_weights(g.f, w);
+    uint32_t v[8];
+#pragma unroll
+    for (uint32_t k = 0; k < 4u; ++k) {
+        v[2 * k] = pick_word(g.q[k], (g.sel >> (4u * k)) & 3u);
+        v[2 * k + 1] = pick_word(g.q[k], (g.sel >> (4u * k + 2u)) & 3u);
+    }
+    return interpolate(v, w);
+}
+
 // Scatter of one level's feature gradient (d0, d1) to the eight corner
 // entries with fp16x2 reductions performed at L2.
 NB_DEV void level_backward(uint32_t* grad, const float p[3], const LevelParams lp, uint32_t hash_mask, float d0, float d1) {

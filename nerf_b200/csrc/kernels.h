@@ -209,7 +209,7 @@ struct OptimArgs {
 cudaError_t launch_wgrad_reduce(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_grad_stats(const OptimArgs& a, cudaStream_t s);
 cudaError_t launch_adam(const OptimArgs& a, cudaStream_t s);
-uint32_t grad_stats_blocks(uint64_t n_params);
+uint32_t grad_stats_blocks(uint64_t n_params, bool fused);
 cudaError_t launch_f32_to_f16(const float* src, void* dst, uint64_t n, cudaStream_t s);
 // dst[i] = scale * draw i of the splitmix64 stream whose state is state0 before
 // the first draw (a uniform in [-1, 1) from the top 24 bits of each draw).

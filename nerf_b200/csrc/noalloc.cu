@@ -69,6 +69,8 @@ NERF_API NerfStatus nerf_b200_field_backward_noalloc(const NerfB200GridLayout* l
     if (!layout || layout->n_levels != 16u || !params || !mlp_grad || !grid_grad) return NERF_STATUS_INVALID_USAGE;
     if (n && (!pos || !dirs || !feat || !dout)) return NERF_STATUS_INVALID_USAGE;
     if (n > 0x7FFFFFFFu) return NERF_STATUS_INVALID_USAGE;  // rows are indexed with 32-bit tile counters
+    // The tables are read and reduced in 16-byte blocks.
+    if ((reinterpret_cast<uintptr_t>(params) & 15u) || (reinterpret_cast<uintptr_t>(grid_grad) & 15u)) return NERF_STATUS_INVALID_USAGE;
     if (nb::ensure_attributes() != cudaSuccess) return NERF_STATUS_CUDA_ERROR;
     // Same CTA count as nerf_b200_field_backward, so both give the same sums.
     const uint32_t blocks = nb::field_backward_blocks();

@@ -505,10 +505,23 @@ uint32_t sm_count() {
 
 }  // namespace
 
-uint32_t grad_stats_blocks(uint64_t n_params) {
+// Blocks of the statistics kernel's parameter part: as many as are resident
+// beside the weight-gradient blocks (fused form), so that the whole grid is
+// one wave -- a second wave of a few blocks would take as long as the first.
+uint32_t grad_stats_blocks(uint64_t n_params, bool fused) {
+    static const int per_sm = [] {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k_grad_stats, 256, 0) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = 4;
+        }
+        return n;
+    }();
     const uint64_t chunks = n_params / 8u;
     const uint64_t want = (chunks + 255u) / 256u;
-    const uint64_t cap = 4ull * sm_count();
+    const uint64_t resident = static_cast<uint64_t>(per_sm) * sm_count();
+    uint64_t cap = resident;
+    if (fused) cap = resident >= kWgradBlocks + sm_count() ? resident - kWgradBlocks : sm_count();
     return static_cast<uint32_t>(want < cap ? (want == 0 ? 1 : want) : cap);
 }
 

@@ -120,6 +120,27 @@ def test_null_arguments_are_invalid_usage_without_a_device():
     assert lib.nerf_create_context(C.byref(desc), C.byref(out)) == abi.NERF_STATUS_INVALID_USAGE
 
 
+def test_misaligned_tables_are_invalid_usage_without_a_device():
+    """Kernel-level entry points refuse parameter / gradient tables that do not
+    start on a 16-byte boundary before any device work (the pointers here are
+    never dereferenced)."""
+    lib = abi.load()
+    g = abi.NerfB200GridLayout()
+    assert lib.nerf_b200_grid_layout(16, 15, 16, 2048, C.byref(g)) == abi.NERF_STATUS_OK
+    ok, bad = C.c_void_p(0x10000), C.c_void_p(0x10008)
+    pos = C.cast(ok, C.POINTER(C.c_float))
+    fl = C.cast(ok, C.POINTER(C.c_float))
+    inv = abi.NERF_STATUS_INVALID_USAGE
+    assert lib.nerf_b200_grid_forward(C.byref(g), pos, 1, bad, ok, None) == inv
+    assert lib.nerf_b200_grid_backward(C.byref(g), pos, 1, ok, bad, None) == inv
+    assert lib.nerf_b200_field_forward(C.byref(g), bad, pos, pos, 1, ok, fl, None) == inv
+    assert lib.nerf_b200_field_backward(C.byref(g), bad, pos, pos, 1, ok, fl, ok, fl, fl, None) == inv
+    assert lib.nerf_b200_field_backward(C.byref(g), ok, pos, pos, 1, ok, fl, bad, fl, fl, None) == inv
+    assert lib.nerf_b200_field_backward_noalloc(C.byref(g), ok, pos, pos, 1, ok, fl, bad, fl, None) == inv
+    assert lib.nerf_b200_mlp_forward(bad, ok, pos, 1, fl, None) == inv
+    assert lib.nerf_b200_mlp_backward(bad, ok, pos, 1, fl, ok, fl, fl, None) == inv
+
+
 def test_scene_generator_is_deterministic_and_sane():
     a = nerf_b200.make_scene(kind=0, seed=0, n_views=4, width=32, height=32, n_threads=2)
     b = nerf_b200.make_scene(kind=0, seed=0, n_views=4, width=32, height=32, n_threads=3)
