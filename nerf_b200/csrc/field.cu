@@ -14,11 +14,13 @@
 // of one layer is the A fragment of the next.
 //
 // The backward kernel recomputes the forward from the stored hash features,
-// back-propagates through both MLPs, scatters the feature gradient into the
-// hash table with fp16x2 reductions, and accumulates the weight gradients of
-// all five matrices over its tiles in registers (each warp owns a fixed fifth
-// of the 10240 weights); the per-CTA sums go to a partials buffer reduced by
-// launch_wgrad_reduce.
+// back-propagates through both MLPs and accumulates the weight gradients of
+// all five matrices over its tiles in registers (each warp owns a fixed
+// quarter of the 10240 weights); the per-CTA sums go to a partials buffer,
+// reduced by the statistics kernel (one GPU) or launch_wgrad_reduce.  The
+// feature gradient goes to the hash table with fp16x2 reductions: from a
+// separate kernel over the training rows (k_grid_scatter), in the kernel
+// itself for the kernel-level entry points.
 #include "grid.cuh"
 #include "kernels.h"
 #include "ray.cuh"

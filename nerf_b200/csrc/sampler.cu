@@ -9,15 +9,16 @@
 // separated from everything that can run in parallel:
 //   k_march        one thread per ray: the ray, its chord and the step
 //                  recurrence, writing t at the start of every 32-step chunk;
-//   k_sample_bits  one warp per ray, lane c walks the 32 steps of chunk c
-//                  from its stored start, testing each midpoint against the
-//                  bitfield, then stores t of every kept step in the ray's
-//                  kept list (in step order) and the ray's count;
+//   k_sample_bits  a 128-thread block per ray, thread k on steps 8k..8k+7
+//                  from the stored start of their chunk, testing each
+//                  midpoint against the bitfield, then storing t of every
+//                  kept step in the ray's kept list (in step order) and the
+//                  ray's count;
 //   k_sample_scan  ordered exclusive scans of counts and active flags with
 //                  the capacity cut;
-//   k_sample_write one warp per kept ray: samples at their final offsets,
-//                  one sample per lane from the kept list, then the ray
-//                  record with its ground-truth colour.
+//   k_sample_write a 128-thread block per kept ray: samples at their final
+//                  offsets from the kept list, then the ray record with its
+//                  ground-truth colour.
 // All float arithmetic that decides which steps are kept uses explicit
 // rounding intrinsics, so the CPU oracle reproduces per-ray counts and
 // offsets bit for bit.  (The reference normalises with the approximate
