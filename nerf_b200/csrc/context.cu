@@ -12,10 +12,13 @@
 //                   backward kernel's weight-gradient partials, the
 //                   occupancy query window
 // The training step is one CUDA graph captured at configure time: occupancy
-// query -> occupancy update -> sampler (count, write) -> field forward ->
-// composite + loss -> field backward -> weight-gradient reduce ->
-// [NCCL all-reduce of gradients and loss when data parallel] -> gradient
-// statistics / step commit -> Adam.  Every kernel reads the step number and
+// query -> occupancy update -> sampler (bitfield tests, scan, sample writes)
+// -> field forward -> composite + loss -> MLP backward -> hash-table scatter
+// -> [data parallel: weight-gradient reduce, then the gradient exchange --
+// peer mode: barrier, owned-range reduce over NVLink, barrier; or an NCCL
+// all-reduce] -> gradient statistics / step commit -> the next step's march
+// -> Adam [peer mode: writing every rank's mirror, then a barrier].  Every
+// kernel reads the step number and
 // the batch sizes from device memory, so nerf_train_step is one
 // cudaGraphLaunch (reference backend-cuda.cu:2405-2420).
 #include <cuda_runtime.h>
